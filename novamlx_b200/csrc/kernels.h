@@ -1,0 +1,109 @@
+// Internal kernel-launch interface of libnovamlx_cuda (host side).
+#pragma once
+
+#include "common.cuh"
+
+namespace nmx {
+
+enum Epi { EPI_STORE = 0, EPI_RESID = 1, EPI_SILU = 2, EPI_ARGMAX = 3 };
+// The argmax epilogue uses at most this many CTAs per SM; its partial
+// buffers hold 32 rows × kArgmaxMaxGridPerSm × SMs entries.
+constexpr int kArgmaxMaxGridPerSm = 4;
+
+// y[M, N] = epilogue( norm?(x)[M, K] · dequant(W)[rows, K]^T )
+struct GemvArgs {
+  const void* x = nullptr;  // [M, K] activations (dtype)
+  long ldx = 0;
+  const void* gamma = nullptr;  // RMSNorm weight [K]; null → x used as is
+  float eps = 1e-5f;
+  const uint32_t* w = nullptr;  // packed [rows, K*bits/32]
+  const void* s = nullptr;      // [rows, K/gs]
+  const void* b = nullptr;
+  // weights are not written by any kernel of this stream's step: the first
+  // k-batch may be requested before griddepcontrol.wait (model forward only)
+  bool weights_static = false;
+  int N = 0, K = 0, M = 0;
+  long pair_off = 0;            // EPI_SILU: up rows start at this row index
+  const void* bias = nullptr;   // [N] added after rounding (qkv bias)
+  void* y = nullptr;            // [M, ldy]
+  long ldy = 0;
+  const void* res = nullptr;    // EPI_RESID: y = rnd(res + rnd(acc)); may alias y
+  long ldres = 0;
+  // EPI_ARGMAX
+  void* logits = nullptr;       // optional [M, N] rounded logits in dtype
+  float* logits_f32 = nullptr;  // optional [M, N] fp32 copy of the rounded logits
+  float* part_val = nullptr;    // [M, grid] scratch
+  int* part_idx = nullptr;
+  unsigned* counter = nullptr;  // zero on entry, left zero on exit
+  int* out_ids = nullptr;       // [M]
+  int* next_tokens = nullptr;   // optional second copy of out_ids
+};
+
+// Launch the quantized GEMV; M rows are processed in chunks the kernel's
+// shared-memory staging can hold. EPI_ARGMAX requires M <= 32 (one chunk).
+nmx_status_t qgemv(Ctx* c, const GemvArgs& a, int bits, int gs, nmx_dtype_t dt, int epi);
+// Largest M one qgemv launch handles for this K (0 when K is too large).
+int qgemv_max_m(int K, int gs);
+
+// ---- attention
+struct AttnArgs {
+  const void* q = nullptr;     // FUSED: qkv rows [T, ldq] (pre-RoPE q|k|v); else q [T, Hq*D] roped
+  long ldq = 0;
+  void* k_cache = nullptr;     // [NB][Hkv][BT][D]
+  void* v_cache = nullptr;
+  const int* block_tables = nullptr;  // [n_seqs][max_blocks]
+  int max_blocks = 0;
+  const int* tok_seq = nullptr;  // [T] sequence index of each query row
+  const int* tok_pos = nullptr;  // [T] absolute position of each query row
+  const float* inv_freq = nullptr;  // [D/2] (FUSED only)
+  void* out = nullptr;         // [T, Hq*D]
+  float* part_o = nullptr;     // [T][Hq][S][D]
+  float* part_ml = nullptr;    // [T][Hq][S][2]
+  unsigned* counters = nullptr;  // [T][Hkv]
+  int T = 0, Hq = 0, Hkv = 0, D = 0, BT = 16;
+  int splits = 1;
+  float scale = 1.0f;
+};
+// fused = 1: apply RoPE to q and append the row's own k/v (one query row per
+// sequence, decode); fused = 0: q is already roped and K/V already appended.
+nmx_status_t paged_attention(Ctx* c, const AttnArgs& a, bool fused);
+
+// RoPE q and k of T new tokens in place in qkv [T, ldq] and write k/v to the
+// pages at each token's position.
+nmx_status_t rope_append(Ctx* c, void* qkv, long ldq, int T, int Hq, int Hkv, int D,
+                         const int* tok_seq, const int* tok_pos, const int* block_tables,
+                         int max_blocks, int BT, void* k_cache, void* v_cache,
+                         const float* inv_freq, void* q_out, long ldqo);
+
+nmx_status_t quantized_sdpa(Ctx* c, const void* q, const uint32_t* kw, const void* ks,
+                            const void* kb, const uint32_t* vw, const void* vs, const void* vb,
+                            int BH, int gqa, int N, int L, int D, float scale, int gs, int bits,
+                            nmx_dtype_t dt, void* out);
+
+// ---- small ops
+nmx_status_t rmsnorm(Ctx* c, const void* x, long ldx, const void* g, int M, int H, float eps,
+                     nmx_dtype_t dt, void* y, long ldy);
+nmx_status_t embed_rows(Ctx* c, const void* table, const int* ids, int T, int H, void* out);
+nmx_status_t argmax_rows(Ctx* c, const void* logits, int M, int V, nmx_dtype_t dt, int* out);
+nmx_status_t penalized_argmax(Ctx* c, const void* logits, int M, int V, nmx_dtype_t dt,
+                              const int* recent, const int* n_recent, int max_recent,
+                              float penalty, int* out);
+nmx_status_t quantize(Ctx* c, const float* w, int N, int K, int bits, int gs, nmx_dtype_t sdt,
+                      uint32_t* wq, void* s, void* b);
+nmx_status_t dequantize(Ctx* c, const uint32_t* wq, const void* s, const void* b, int N, int K,
+                        int bits, int gs, nmx_dtype_t sdt, float* w);
+// generate N(0, std) for rows [N, K] from (seed, stream_id) and quantize in one pass
+nmx_status_t random_quantized(Ctx* c, uint64_t seed, uint64_t stream_id, float std, int N, int K,
+                              int bits, int gs, nmx_dtype_t sdt, uint32_t* wq, void* s, void* b);
+nmx_status_t random_fill(Ctx* c, uint64_t seed, uint64_t stream_id, float std, float mean,
+                         size_t n, nmx_dtype_t dt, void* out);
+nmx_status_t fill_value(Ctx* c, size_t n, float v, nmx_dtype_t dt, void* out);
+nmx_status_t copy_kv_blocks(Ctx* c, void* base, long layer_stride_bytes, int layers,
+                            long block_bytes, const int* src, const int* dst, int n);
+// seq[b] = b, pos[b] = lens[b] - 1 (one query row per sequence)
+nmx_status_t seq_rows_from_lens(Ctx* c, const int* lens, int B, int* seq, int* pos);
+// decode bookkeeping after a step: pos[b] += 1; history[step * B + b] = tok[b]
+// while (step + 1) * B <= hist_cap; step++
+nmx_status_t decode_advance(Ctx* c, int* pos, const int* tok, int B, int* history, int hist_cap, int* step);
+
+}  // namespace nmx

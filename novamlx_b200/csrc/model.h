@@ -1,0 +1,112 @@
+// Model and KV-pool objects behind the nmx_model_t / nmx_kv_pool_t handles.
+#pragma once
+
+#include <map>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "common.cuh"
+
+namespace nmx {
+
+struct Lin {
+  uint32_t* w = nullptr;  // packed [N, K*bits/32]
+  void* s = nullptr;      // [N, K/gs]
+  void* b = nullptr;
+  int N = 0, K = 0;
+};
+
+struct LayerW {
+  void* attn_norm = nullptr;
+  void* mlp_norm = nullptr;
+  Lin qkv;                  // rows: q | k | v
+  void* qkv_bias = nullptr;
+  Lin o;
+  Lin gu;                   // rows: gate | up
+  Lin down;
+};
+
+struct GraphEntry {
+  cudaGraphExec_t exec = nullptr;
+  size_t nodes = 0;
+};
+
+struct KvPool;
+
+struct Model {
+  Ctx* ctx = nullptr;
+  nmx_model_cfg cfg{};
+  nmx_dtype_t dt = NMX_F16;
+  int max_batch = 1, max_tokens = 1, rows_logits = 1;
+  int Nq = 0, Nkv = 0, Nqkv = 0;
+  char* wbase = nullptr;
+  size_t wbytes = 0;
+  uint64_t step_bytes = 0;
+  void* embed = nullptr;
+  void* final_norm = nullptr;
+  Lin lm;
+  std::vector<LayerW> layers;
+  bool weights_ready = false, loaded_any = false;
+
+  // workspace
+  char* wsbase = nullptr;
+  void *h = nullptr, *qkv = nullptr, *q_roped = nullptr, *attn = nullptr, *act = nullptr, *last_h = nullptr;
+  float* logits_f32 = nullptr;
+  float *part_o = nullptr, *part_ml = nullptr;
+  unsigned* attn_counters = nullptr;
+  float* am_val = nullptr;
+  int* am_idx = nullptr;
+  unsigned* am_counter = nullptr;
+  int *tok_ids = nullptr, *tok_seq = nullptr, *tok_pos = nullptr, *last_rows = nullptr, *out_ids = nullptr;
+  int *block_tables = nullptr, *hist = nullptr, *step = nullptr;
+  float* inv_freq = nullptr;
+  char* pinned = nullptr;
+  size_t pinned_bytes = 0;
+  int pool_blocks_hint = 0;
+  size_t h2d_bytes_last = 0;
+  std::map<std::pair<int, const void*>, GraphEntry> graphs;
+
+  static nmx_status_t create(Ctx* c, const nmx_model_cfg& cfg, Model** out);
+  ~Model();
+  nmx_status_t init_random(uint64_t seed, float stdv);
+  nmx_status_t resolve(const std::string& name, char** dst, size_t* bytes, std::vector<int64_t>* shape,
+                       nmx_dtype_t* dtype);
+  nmx_status_t load_tensor(const std::string& name, const void* host, nmx_dtype_t dtype, const int64_t* shape,
+                           int ndim);
+  nmx_status_t get_tensor(const std::string& name, void* host, size_t host_bytes);
+
+  nmx_status_t run_layers_decode(KvPool* pool, int B);
+  nmx_status_t run_layers_prefill(KvPool* pool, int T);
+  nmx_status_t run_head(const void* x, int rows, bool want_logits, int* next_tokens);
+  nmx_status_t decode_step_body(KvPool* pool, int B);
+  nmx_status_t run_decode_graph(KvPool* pool, int B);
+  nmx_status_t upload_batch(const nmx_seq_t* seqs, int n, int* T_out, bool* decode_out);
+  nmx_status_t forward(KvPool* pool, const nmx_seq_t* seqs, int n, nmx_out_mode_t mode, void* out_host);
+  nmx_status_t decode_greedy(KvPool* pool, const int32_t* first, const int32_t* start, const int32_t* tables,
+                             int max_blocks, int n, int steps, int32_t* out_host);
+};
+
+struct KvPool {
+  Model* model = nullptr;
+  char* base = nullptr;  // [L][K|V][num_blocks][Hkv][BT][D] f16
+  int num_blocks = 0;
+  size_t block_bytes = 0;   // one block of K (or V) of one layer
+  size_t layer_stride = 0;  // bytes per layer (K and V)
+  static nmx_status_t create(Model* m, int block_tokens, int num_blocks, KvPool** out);
+  ~KvPool();
+  void* k_layer(int l) const { return base + size_t(l) * layer_stride; }
+  void* v_layer(int l) const { return base + size_t(l) * layer_stride + layer_stride / 2; }
+};
+
+}  // namespace nmx
+
+struct nmx_ctx_s {
+  nmx::Ctx c;
+};
+struct nmx_model_s {
+  nmx::Model* m;
+};
+struct nmx_kv_pool_s {
+  nmx::KvPool* p;
+};

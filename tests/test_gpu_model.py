@@ -1,0 +1,195 @@
+"""Model-level GPU parity: the C ABI forward (prefill, decode, device greedy
+loop) against the CPU oracle forward on the same random-init weights.
+Bars (workload definition): logits cosine >= 0.999 and max_rel_err <= 2e-2
+vs the fp32-dequant oracle; greedy ids bit-exact given identical logits;
+page/block indexing bit-exact (permuted tables, prefix hits)."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def tiny_cfgs():
+    from novamlx_b200 import nmx
+    llama = dict(vocab=1024, hidden=512, n_layers=2, n_heads=8, n_kv_heads=2, head_dim=64, ffn=1024,
+                 rope_theta=500000.0, rope_factor=8.0, rope_low_freq_factor=1.0, rope_high_freq_factor=4.0,
+                 rope_original_max_pos=64, rms_eps=1e-5)
+    qwen = dict(vocab=1024, hidden=512, n_layers=2, n_heads=4, n_kv_heads=2, head_dim=128, ffn=1536,
+                qkv_bias=True, rope_theta=1e6, rms_eps=1e-6)
+    l8 = dict(llama, bits=8, group_size=32)
+    return {"llama": llama, "qwen": qwen, "llama8": l8}
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    from novamlx_b200 import nmx
+    return nmx.Context(0)
+
+
+def build(ctx, name, seed=1, max_batch=8, max_tokens=512):
+    from novamlx_b200 import nmx
+    d = tiny_cfgs()[name]
+    ocfg = O.TinyCfg(**d)
+    tensors = O.random_tensors(ocfg, seed=seed, std=0.05)
+    cfg = nmx.ModelConfig(**d, max_batch=max_batch, max_tokens=max_tokens)
+    m = nmx.Model(ctx, cfg)
+    for k, v in tensors.items():
+        m.load_tensor(k, v.view(np.float16) if v.dtype == np.uint16 else v)
+    return m, O.OracleModel(ocfg, tensors), cfg
+
+
+def check_logits(got, ref):
+    for g, r in zip(np.atleast_2d(got), np.atleast_2d(ref)):
+        assert O.cosine(g, r) >= 0.999
+        assert O.max_rel_err(g, r) <= 2e-2
+
+
+@pytest.mark.parametrize("name", ["llama", "qwen", "llama8"])
+def test_prefill_and_decode_match_oracle(ctx, name):
+    from novamlx_b200 import nmx
+    m, om, cfg = build(ctx, name)
+    pool = nmx.KVPool(m, 64)
+    rng = np.random.default_rng(3)
+    prompt = rng.integers(0, cfg.vocab, 45)
+    table = rng.permutation(64)[:8].astype(np.int32)  # 128 tokens of pages, shuffled
+    got = m.forward(pool, [dict(tokens=prompt, start_pos=0, block_table=table)], nmx.OUT_LOGITS_ALL)
+    cache = om.new_cache(128)
+    ref = om.forward(cache, prompt, 0, all_logits=True)
+    check_logits(got, ref)
+    # teacher-forced decode steps through the fused decode path
+    pos = len(prompt)
+    for step in range(6):
+        tok = int(rng.integers(0, cfg.vocab))
+        g = m.forward(pool, [dict(tokens=[tok], start_pos=pos, block_table=table)], nmx.OUT_LOGITS_LAST)
+        r = om.forward(cache, [tok], pos)
+        check_logits(g, r)
+        ids = m.forward(pool, [dict(tokens=[tok], start_pos=pos, block_table=table)], nmx.OUT_ARGMAX_LAST)
+        assert ids[0] == int(np.argmax(g[0]))  # same logits → same id, lowest index on ties
+        pos += 1
+
+
+def test_batched_decode_and_ragged_prefill(ctx):
+    """A mixed batch (prefill chunks of different lengths) and a batched
+    decode step equal the per-sequence oracle."""
+    from novamlx_b200 import nmx
+    m, om, cfg = build(ctx, "llama")
+    pool = nmx.KVPool(m, 96)
+    rng = np.random.default_rng(5)
+    lens = [3, 40, 17, 1]
+    prompts = [rng.integers(0, cfg.vocab, n) for n in lens]
+    perm = rng.permutation(96).astype(np.int32)
+    tables = [perm[8 * i:8 * (i + 1)] for i in range(4)]
+    got = m.forward(pool, [dict(tokens=p, start_pos=0, block_table=t) for p, t in zip(prompts, tables)],
+                    nmx.OUT_LOGITS_LAST)
+    caches = [om.new_cache(128) for _ in lens]
+    for i, p in enumerate(prompts):
+        check_logits(got[i], om.forward(caches[i], p, 0))
+    toks = rng.integers(0, cfg.vocab, 4)
+    got = m.forward(pool, [dict(tokens=[t], start_pos=n, block_table=tb) for t, n, tb in zip(toks, lens, tables)],
+                    nmx.OUT_LOGITS_LAST)
+    for i in range(4):
+        check_logits(got[i], om.forward(caches[i], [toks[i]], lens[i]))
+
+
+def test_prefix_hit_equals_full_prefill(ctx):
+    """Prefill of 48 tokens == prefill of the first 32 (a cached prefix,
+    two full 16-token blocks) + the remaining 16 on top of those pages."""
+    from novamlx_b200 import nmx
+    m, _, cfg = build(ctx, "llama")
+    pool = nmx.KVPool(m, 32)
+    rng = np.random.default_rng(6)
+    prompt = rng.integers(0, cfg.vocab, 48)
+    t1 = np.array([3, 9, 4, 20], np.int32)
+    full = m.forward(pool, [dict(tokens=prompt, start_pos=0, block_table=t1)], nmx.OUT_LOGITS_LAST)
+    t2 = np.array([11, 7, 25, 1], np.int32)
+    m.forward(pool, [dict(tokens=prompt[:32], start_pos=0, block_table=t2)], nmx.OUT_LOGITS_LAST)
+    hit = m.forward(pool, [dict(tokens=prompt[32:], start_pos=32, block_table=t2)], nmx.OUT_LOGITS_LAST)
+    assert np.array_equal(full, hit)
+
+
+def test_block_table_permutation_and_copy(ctx):
+    from novamlx_b200 import nmx
+    m, _, cfg = build(ctx, "qwen")
+    pool = nmx.KVPool(m, 40)
+    rng = np.random.default_rng(7)
+    prompt = rng.integers(0, cfg.vocab, 50)
+    a = m.forward(pool, [dict(tokens=prompt, start_pos=0, block_table=[0, 1, 2, 3])], nmx.OUT_LOGITS_LAST)
+    b = m.forward(pool, [dict(tokens=prompt, start_pos=0, block_table=[33, 5, 17, 2])], nmx.OUT_LOGITS_LAST)
+    assert np.array_equal(a, b)
+    # copy-on-write: duplicate the pages of table A and decode from the copies
+    pool.copy_blocks([0, 1, 2, 3], [20, 21, 22, 23])
+    tok = [int(rng.integers(0, cfg.vocab))]
+    x = m.forward(pool, [dict(tokens=tok, start_pos=50, block_table=[0, 1, 2, 3])], nmx.OUT_LOGITS_LAST)
+    y = m.forward(pool, [dict(tokens=tok, start_pos=50, block_table=[20, 21, 22, 23])], nmx.OUT_LOGITS_LAST)
+    assert np.array_equal(x, y)
+
+
+def test_decode_greedy_loop_equals_host_loop(ctx):
+    from novamlx_b200 import nmx
+    m, om, cfg = build(ctx, "llama")
+    pool = nmx.KVPool(m, 80)
+    rng = np.random.default_rng(8)
+    B, P, S = 3, 20, 12
+    prompts = [rng.integers(0, cfg.vocab, P) for _ in range(B)]
+    tables = rng.permutation(80)[:B * 4].astype(np.int32).reshape(B, 4)
+    first = m.forward(pool, [dict(tokens=p, start_pos=0, block_table=t) for p, t in zip(prompts, tables)],
+                      nmx.OUT_ARGMAX_LAST)
+    dev_ids = m.decode_greedy(pool, first, [P] * B, tables, S)
+    # host loop through nmx_forward (decode graph) over the same pages
+    m.forward(pool, [dict(tokens=p, start_pos=0, block_table=t) for p, t in zip(prompts, tables)],
+              nmx.OUT_ARGMAX_LAST)
+    cur = first.copy()
+    host = []
+    for s in range(S):
+        cur = m.forward(pool, [dict(tokens=[cur[i]], start_pos=P + s, block_table=tables[i]) for i in range(B)],
+                        nmx.OUT_ARGMAX_LAST)
+        host.append(cur.copy())
+    assert np.array_equal(dev_ids, np.stack(host))
+    # and the oracle, teacher-forced on the GPU's ids, agrees on most steps
+    agree = 0
+    for i in range(B):
+        c = om.new_cache(64)
+        r = om.forward(c, prompts[i], 0)
+        agree += int(np.argmax(r[0]) == first[i])
+        for s in range(S - 1):
+            tok = dev_ids[s, i]
+            r = om.forward(c, [tok], P + s)
+            agree += int(np.argmax(r[0]) == dev_ids[s + 1, i])
+    assert agree >= int(0.9 * B * S)
+
+
+def test_forward_rejects_bad_inputs(ctx):
+    from novamlx_b200 import nmx
+    m, _, cfg = build(ctx, "llama")
+    pool = nmx.KVPool(m, 8)
+    with pytest.raises(nmx.NmxError) as e:
+        m.forward(pool, [dict(tokens=[1, 2], start_pos=0, block_table=[99])])
+    assert e.value.status == nmx.NMX_ERR_INVALID
+    with pytest.raises(nmx.NmxError):
+        m.forward(pool, [dict(tokens=list(range(20)), start_pos=0, block_table=[0])])  # table too short
+    with pytest.raises(nmx.NmxError):
+        m.forward(pool, [dict(tokens=[cfg.vocab], start_pos=0, block_table=[0])])  # token out of range
+
+
+def test_tensor_roundtrip(ctx):
+    m, _, cfg = build(ctx, "qwen")
+    w = m.get_tensor("model.layers.1.self_attn.k_proj.weight", (256, 512 * 4 // 32), np.uint32)
+    ref = O.random_tensors(O.TinyCfg(**tiny_cfgs()["qwen"]), seed=1, std=0.05)
+    assert np.array_equal(w, ref["model.layers.1.self_attn.k_proj.weight"])
+    b = m.get_tensor("model.layers.0.self_attn.v_proj.bias", (256,), np.uint16)
+    assert np.array_equal(b, ref["model.layers.0.self_attn.v_proj.bias"])
+
+
+def test_random_init_model_runs(ctx):
+    """nmx_model_init_random + greedy decode at the 8B head/ffn widths but 2 layers."""
+    from novamlx_b200 import nmx
+    cfg = nmx.llama31_8b(n_layers=2, max_batch=2, max_tokens=256)
+    m = nmx.Model(ctx, cfg)
+    m.init_random(seed=0, std=0.02)
+    pool = nmx.KVPool(m, 32)
+    prompt = np.random.default_rng(0).integers(0, cfg.vocab, 100)
+    first = m.forward(pool, [dict(tokens=prompt, start_pos=0, block_table=np.arange(16))])
+    ids = m.decode_greedy(pool, first, [100], np.arange(16)[None], 20)
+    assert ids.shape == (20, 1) and np.all((ids >= 0) & (ids < cfg.vocab))
