@@ -92,15 +92,29 @@ NMX_API nmx_status_t nmx_ctx_create(int device, nmx_ctx_t* out) {
   return NMX_OK;
 }
 
-NMX_API nmx_status_t nmx_ctx_destroy(nmx_ctx_t ctx) {
-  API_BEGIN;
-  if (!ctx) return NMX_OK;
+static void ctx_release(nmx_ctx_t ctx) {
+  if (--ctx->refs > 0) return;
   cudaSetDevice(ctx->c.device);
   if (ctx->c.stream) cudaStreamSynchronize(ctx->c.stream);
   if (ctx->c.ws) cudaFree(ctx->c.ws);
   if (ctx->c.counters) cudaFree(ctx->c.counters);
   if (ctx->c.owns_stream && ctx->c.stream) cudaStreamDestroy(ctx->c.stream);
   delete ctx;
+}
+
+static void model_release(nmx_model_t model) {
+  if (--model->refs > 0) return;
+  cudaStreamSynchronize(model->m->ctx->stream);
+  delete model->m;
+  nmx_ctx_s* ctx = model->ctx;
+  delete model;
+  ctx_release(ctx);
+}
+
+NMX_API nmx_status_t nmx_ctx_destroy(nmx_ctx_t ctx) {
+  API_BEGIN;
+  if (!ctx) return NMX_OK;
+  ctx_release(ctx);
   return NMX_OK;
 }
 
@@ -284,16 +298,15 @@ NMX_API nmx_status_t nmx_model_create(nmx_ctx_t ctx, const nmx_model_cfg* cfg, n
   NMX_CUDA_OK(cudaSetDevice(ctx->c.device));
   Model* m = nullptr;
   NMX_TRY(Model::create(&ctx->c, *cfg, &m));
-  *out = new nmx_model_s{m};
+  ctx->refs++;
+  *out = new nmx_model_s{m, ctx};
   return NMX_OK;
 }
 
 NMX_API nmx_status_t nmx_model_destroy(nmx_model_t model) {
   API_BEGIN;
   if (!model) return NMX_OK;
-  cudaStreamSynchronize(model->m->ctx->stream);
-  delete model->m;
-  delete model;
+  model_release(model);
   return NMX_OK;
 }
 
@@ -330,7 +343,8 @@ NMX_API nmx_status_t nmx_kv_pool_create(nmx_model_t model, int block_tokens, int
   REQUIRE(out, "output handle");
   KvPool* p = nullptr;
   NMX_TRY(KvPool::create(model->m, block_tokens, num_blocks, &p));
-  *out = new nmx_kv_pool_s{p};
+  model->refs++;
+  *out = new nmx_kv_pool_s{p, model};
   return NMX_OK;
 }
 
@@ -339,7 +353,9 @@ NMX_API nmx_status_t nmx_kv_pool_destroy(nmx_kv_pool_t pool) {
   if (!pool) return NMX_OK;
   cudaStreamSynchronize(pool->p->model->ctx->stream);
   delete pool->p;
+  nmx_model_s* model = pool->model;
   delete pool;
+  model_release(model);
   return NMX_OK;
 }
 

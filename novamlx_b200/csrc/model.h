@@ -101,12 +101,18 @@ struct KvPool {
 
 }  // namespace nmx
 
+// Handles are reference counted: a model keeps its context alive and a pool
+// keeps its model alive, so destroying handles in any order is safe.
 struct nmx_ctx_s {
   nmx::Ctx c;
+  int refs = 1;
 };
 struct nmx_model_s {
   nmx::Model* m;
+  nmx_ctx_s* ctx;
+  int refs = 1;
 };
 struct nmx_kv_pool_s {
   nmx::KvPool* p;
+  nmx_model_s* model;
 };

@@ -40,6 +40,7 @@ namespace nmx {
 namespace {
 
 constexpr int kThreads = 256;
+constexpr int kMaxDynSmem = 210 * 1024;  // dynamic smem ceiling of every qgemv launch
 constexpr int kWarps = kThreads / 32;
 
 template <int BITS, int GS>
@@ -508,20 +509,26 @@ nmx_status_t launch_one(Ctx* c, const GemvArgs& a, int M) {
                       size_t(TPC * KS * 16 * NCOL + 16 * TPC * NCOL) * sizeof(float);
   auto kern = qgemv_kernel<T, BITS, GS, NT, EPI, TPC>;
   static std::mutex mu;
+  static std::map<int, bool> attr_set;                // device → max smem attribute raised
   static std::map<std::pair<int, size_t>, int> occ;  // (device, smem) → CTAs per SM
   int per_sm = 0;
   {
     std::lock_guard<std::mutex> lk(mu);
+    if (!attr_set[c->device]) {
+      // raise the kernel's limit once to the largest size any launch uses
+      NMX_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem));
+      attr_set[c->device] = true;
+    }
     auto key = std::make_pair(c->device, smem);
     auto itr = occ.find(key);
     if (itr == occ.end()) {
-      NMX_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
       NMX_CUDA_OK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem));
       occ[key] = per_sm;
     } else {
       per_sm = itr->second;
     }
   }
+  NMX_CHECK(smem <= size_t(kMaxDynSmem), NMX_ERR_UNSUPPORTED, "qgemv: shared-memory staging too large");
   NMX_CHECK(per_sm > 0, NMX_ERR_UNSUPPORTED, "qgemv: configuration does not fit on an SM");
   const int rows_per_tg = (EPI == EPI_SILU) ? 16 : 16 * TPC;
   const int num_tg = a.N / rows_per_tg;

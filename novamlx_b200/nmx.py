@@ -15,6 +15,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import sys
 from dataclasses import dataclass, field
 from pathlib import Path
 from typing import Optional, Sequence
@@ -205,6 +206,8 @@ class Context:
             self.h = None
 
     def __del__(self):
+        if sys.is_finalizing():
+            return  # the process is exiting; the driver reclaims device memory
         try:
             self.close()
         except Exception:
@@ -372,6 +375,8 @@ class Model:
             self.h = None
 
     def __del__(self):
+        if sys.is_finalizing():
+            return  # the process is exiting; the driver reclaims device memory
         try:
             self.close()
         except Exception:
@@ -485,6 +490,8 @@ class KVPool:
             self.h = None
 
     def __del__(self):
+        if sys.is_finalizing():
+            return  # the process is exiting; the driver reclaims device memory
         try:
             self.close()
         except Exception:
@@ -525,7 +532,7 @@ class PagedBlockPool:
         self.block_size = block_size
 
     def __del__(self):
-        if getattr(self, "h", None):
+        if getattr(self, "h", None) and not sys.is_finalizing():
             lib.nmx_block_pool_destroy(self.h)
             self.h = None
 

@@ -153,11 +153,12 @@ def test_decode_greedy_loop_equals_host_loop(ctx):
         c = om.new_cache(64)
         r = om.forward(c, prompts[i], 0)
         agree += int(np.argmax(r[0]) == first[i])
-        for s in range(S - 1):
-            tok = dev_ids[s, i]
+        tok = first[i]
+        for s in range(S):
             r = om.forward(c, [tok], P + s)
-            agree += int(np.argmax(r[0]) == dev_ids[s + 1, i])
-    assert agree >= int(0.9 * B * S)
+            agree += int(np.argmax(r[0]) == dev_ids[s, i])
+            tok = dev_ids[s, i]
+    assert agree >= int(0.9 * B * (S + 1))
 
 
 def test_forward_rejects_bad_inputs(ctx):
