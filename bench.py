@@ -363,6 +363,7 @@ def _run_ours(args, rank, world, dist, torch, nmx, ctx, peaks, dev):
 
 
 def main():
+    global PROMPT, GEN
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
@@ -370,7 +371,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (profiling runs only)")
+    ap.add_argument("--gen", type=int, default=GEN, help="tokens per step (profiling runs only)")
     args = ap.parse_args()
+    PROMPT, GEN = args.prompt, args.gen
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":

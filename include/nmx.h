@@ -92,6 +92,22 @@ NMX_API nmx_status_t nmx_op_qmatmul(nmx_ctx_t ctx, const void* x, const uint32_t
                                     int K, int bits, int group_size, int transpose,
                                     nmx_dtype_t dtype, void* y);
 
+/* Repack an MLX-layout 4-bit group-64 fp16 linear (wq u32[N, K/8], scales
+ * and biases f16[N, K/64]) into decode records: 1152-byte records of 16 rows
+ * x 128 k (packed words in MMA-fragment order, then the 2x16 scales and
+ * biases), the layout the model streams in its decode GEMV. `records` holds
+ * N*K*9/16 bytes (the same bytes as the three MLX arrays). N % 16 == 0,
+ * K % 128 == 0. Same operator as MLX.quantizedMM's weights
+ * (Sources/NovaMLXEngine/Models/BailingHybridModel.swift:213), stored for
+ * streaming. */
+NMX_API nmx_status_t nmx_op_pack_records(nmx_ctx_t ctx, const uint32_t* wq, const void* scales,
+                                         const void* biases, int N, int K, void* records);
+/* y[M,N] = x[M,K] · dequant(W)^T for W held as decode records (see
+ * nmx_op_pack_records); fp16 in/out, fp32 accumulation. Same arithmetic as
+ * nmx_op_qmatmul on the MLX-layout weights. */
+NMX_API nmx_status_t nmx_op_qmatmul_records(nmx_ctx_t ctx, const void* x, const void* records, int M,
+                                            int N, int K, void* y);
+
 /* Affine quantization of fp32 W[N,K] along K: per group, scale =
  * (max-min)/(2^bits-1), bias = min, q = clamp(rint((w-bias)/scale), 0,
  * 2^bits-1) computed with the fp32 scale/bias, which are then stored in

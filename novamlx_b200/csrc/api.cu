@@ -168,6 +168,42 @@ NMX_API nmx_status_t nmx_op_qmatmul(nmx_ctx_t ctx, const void* x, const uint32_t
   return qgemv(&ctx->c, a, bits, group_size, dtype, EPI_STORE);
 }
 
+NMX_API nmx_status_t nmx_op_pack_records(nmx_ctx_t ctx, const uint32_t* wq, const void* scales, const void* biases,
+                                         int N, int K, void* records) {
+  API_BEGIN;
+  REQUIRE(ctx, "context");
+  if (N == 0) return NMX_OK;
+  REQUIRE(wq, "wq");
+  REQUIRE(scales, "scales");
+  REQUIRE(biases, "biases");
+  REQUIRE(records, "records");
+  NMX_CHECK(N % 16 == 0 && K % 128 == 0, NMX_ERR_UNSUPPORTED, "nmx_op_pack_records: N % 16, K % 128");
+  NMX_CHECK(reinterpret_cast<uintptr_t>(records) % 16 == 0, NMX_ERR_INVALID, "records must be 16-byte aligned");
+  return repack_to_records(&ctx->c, wq, scales, biases, N, K, 0, records, 7);
+}
+
+NMX_API nmx_status_t nmx_op_qmatmul_records(nmx_ctx_t ctx, const void* x, const void* records, int M, int N, int K,
+                                            void* y) {
+  API_BEGIN;
+  REQUIRE(ctx, "context");
+  if (M == 0 || N == 0) return NMX_OK;
+  REQUIRE(x, "x");
+  REQUIRE(records, "records");
+  REQUIRE(y, "y");
+  NMX_CHECK(qgemv_dl_supported(4, 64, NMX_F16, N, K), NMX_ERR_UNSUPPORTED, "nmx_op_qmatmul_records: N % 16, K % 128");
+  NMX_CHECK(reinterpret_cast<uintptr_t>(records) % 16 == 0, NMX_ERR_INVALID, "records must be 16-byte aligned");
+  Ctx* c = &ctx->c;
+  GemvDLArgs a;
+  const size_t pf = qgemv_dl_partials_floats(N, K, EPI_STORE, c->num_sms, a.ctas_per_sm);
+  void* ws = nullptr;
+  NMX_TRY(ctx_workspace(c, pf * 4 + 256, &ws));
+  unsigned* ctr = nullptr;
+  NMX_TRY(ctx_counters(c, size_t(N / 16), &ctr));
+  a.x = x; a.ldx = K; a.w = records; a.N = N; a.K = K; a.M = M; a.y = y; a.ldy = N;
+  a.partials = static_cast<float*>(ws); a.partials_cap = pf; a.counters = ctr;
+  return qgemv_dl(c, a, EPI_STORE);
+}
+
 NMX_API nmx_status_t nmx_op_quantize(nmx_ctx_t ctx, const float* w, int N, int K, int bits, int group_size,
                                      nmx_dtype_t sdtype, uint32_t* wq, void* scales, void* biases) {
   API_BEGIN;

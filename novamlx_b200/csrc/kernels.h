@@ -45,6 +45,44 @@ nmx_status_t qgemv(Ctx* c, const GemvArgs& a, int bits, int gs, nmx_dtype_t dt, 
 // Largest M one qgemv launch handles for this K (0 when K is too large).
 int qgemv_max_m(int K, int gs);
 
+// Decode GEMV over decode records (4-bit g64, f16): see qgemv_dl.cu.
+struct GemvDLArgs {
+  const void* x = nullptr;  // [M, K] f16
+  long ldx = 0;
+  const void* gamma = nullptr;
+  float eps = 1e-5f;
+  const void* w = nullptr;  // decode records of the whole matrix
+  int N = 0, K = 0, M = 0;  // N = output columns (gate rows for EPI_SILU)
+  int n_tg = 0;             // set by qgemv_dl
+  long pair_tiles = 0;      // EPI_SILU: tile offset of the up rows
+  const void* bias = nullptr;
+  void* y = nullptr;
+  long ldy = 0;
+  const void* res = nullptr;
+  long ldres = 0;
+  float* logits_f32 = nullptr;        // EPI_ARGMAX: optional [M, N]
+  unsigned long long* keys = nullptr; // EPI_ARGMAX: [32] packed (value, index), zero between launches
+  unsigned* done = nullptr;           // EPI_ARGMAX: finished tile groups, zero between launches
+  int* out_ids = nullptr;
+  int* next_tokens = nullptr;
+  float* partials = nullptr;          // split tile groups' partial sums
+  size_t partials_cap = 0;            // floats
+  int max_contrib = 0;                // slot stride (set per launch)
+  unsigned* counters = nullptr;       // [n_tg], zero between launches
+  int ctas_per_sm = 2;
+};
+bool qgemv_dl_supported(int bits, int gs, nmx_dtype_t dt, int N, int K);
+int qgemv_dl_max_m(int K, int epi);
+// floats of partial-sum scratch one launch of this shape may need
+size_t qgemv_dl_partials_floats(int N_out, int K, int epi, int num_sms, int ctas_per_sm);
+nmx_status_t qgemv_dl(Ctx* c, const GemvDLArgs& a, int epi);
+// MLX-layout parts (mask 1 = words, 2 = scales, 4 = biases) of rows
+// [row0, row0 + rows) to decode records, and back.
+nmx_status_t repack_to_records(Ctx* c, const uint32_t* wq, const void* s, const void* b, int rows, int K,
+                               long row0, void* rec, int part_mask);
+nmx_status_t unpack_from_records(Ctx* c, const void* rec, int rows, int K, long row0, uint32_t* wq, void* s,
+                                 void* b, int part_mask);
+
 // ---- attention
 struct AttnArgs {
   const void* q = nullptr;     // FUSED: qkv rows [T, ldq] (pre-RoPE q|k|v); else q [T, Hq*D] roped

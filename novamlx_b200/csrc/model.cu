@@ -112,12 +112,14 @@ nmx_status_t Model::create(Ctx* c, const nmx_model_cfg& cfg, Model** out) {
   std::vector<std::pair<void**, size_t>> slices;
   size_t total = 0;
   auto plan = [&](void** p, size_t bytes) { slices.push_back({p, bytes}); total += align_up(bytes, 256); };
+  std::vector<Lin*> lins;
   auto plan_lin = [&](Lin& l, int N, int K) {
     l.N = N;
     l.K = K;
-    plan(reinterpret_cast<void**>(&l.w), size_t(N) * K * cfg.bits / 8);
-    plan(&l.s, size_t(N) * (K / gs) * es);
-    plan(&l.b, size_t(N) * (K / gs) * es);
+    l.dl = qgemv_dl_supported(cfg.bits, gs, nmx_dtype_t(cfg.dtype), N, K);
+    l.bytes = size_t(N) * K * cfg.bits / 8 + 2 * size_t(N) * (K / gs) * es;
+    plan(reinterpret_cast<void**>(&l.w), l.bytes);  // words | scales | biases, or decode records
+    lins.push_back(&l);
   };
   m->layers.resize(L);
   plan(&m->embed, size_t(V) * H * es);
@@ -142,6 +144,13 @@ nmx_status_t Model::create(Ctx* c, const nmx_model_cfg& cfg, Model** out) {
   for (auto& s : slices) {
     *s.first = m->wbase + off;
     off += align_up(s.second, 256);
+  }
+  for (Lin* l : lins) {
+    if (l->dl) continue;
+    char* base = reinterpret_cast<char*>(l->w);
+    const size_t wb = size_t(l->N) * l->K * cfg.bits / 8, sb = size_t(l->N) * (l->K / gs) * es;
+    l->s = base + wb;
+    l->b = base + wb + sb;
   }
   // byte counts: everything one decode step reads once
   m->step_bytes = 0;
@@ -184,7 +193,33 @@ nmx_status_t Model::create(Ctx* c, const nmx_model_cfg& cfg, Model** out) {
       {reinterpret_cast<void**>(&m->hist), size_t(kHistCap) * 4},
       {reinterpret_cast<void**>(&m->step), 256},
       {reinterpret_cast<void**>(&m->inv_freq), size_t(cfg.head_dim / 2) * 4},
+      {reinterpret_cast<void**>(&m->dl_partials), 0},
+      {reinterpret_cast<void**>(&m->dl_counters), 0},
+      {reinterpret_cast<void**>(&m->dl_keys), 32 * 8},
+      {reinterpret_cast<void**>(&m->dl_done), 256},
   };
+  {
+    size_t pf = 0, ntg = 1;
+    auto need = [&](const Lin& l, bool paired) {
+      if (!l.dl) return;
+      const int n_out = paired ? l.N / 2 : l.N;
+      pf = std::max(pf, qgemv_dl_partials_floats(n_out, l.K, paired ? EPI_SILU : EPI_STORE, c->num_sms,
+                                                 m->dl_ctas_per_sm));
+      ntg = std::max(ntg, size_t(n_out / 16));
+    };
+    need(m->lm, false);
+    for (const auto& ly : m->layers) {
+      need(ly.qkv, false);
+      need(ly.o, false);
+      need(ly.gu, true);
+      need(ly.down, false);
+    }
+    m->dl_partials_cap = pf;
+    for (auto& w : ws) {
+      if (w.p == reinterpret_cast<void**>(&m->dl_partials)) w.bytes = std::max<size_t>(pf, 1) * 4;
+      if (w.p == reinterpret_cast<void**>(&m->dl_counters)) w.bytes = ntg * 4;
+    }
+  }
   size_t wtot = 0;
   for (auto& w : ws) wtot += align_up(w.bytes, 256);
   st = alloc_dev(reinterpret_cast<void**>(&m->wsbase), wtot);
@@ -233,10 +268,28 @@ nmx_status_t Model::init_random(uint64_t seed, float stdv) {
   const int H = cfg.hidden, F = cfg.ffn, V = cfg.vocab;
   const int bits = cfg.bits, gs = cfg.group_size;
   uint64_t sid = 1;
+  // decode-record linears are generated in MLX layout into a scratch slice
+  // and repacked; the scratch holds the largest slice (the lm_head)
+  size_t tmp_bytes = lm.bytes;
+  for (const auto& ly : layers)
+    for (const Lin* l : {&ly.qkv, &ly.o, &ly.gu, &ly.down}) tmp_bytes = std::max(tmp_bytes, l->bytes);
+  char* tmp = nullptr;
+  NMX_TRY(alloc_dev(reinterpret_cast<void**>(&tmp), tmp_bytes));
+  struct TmpFree {
+    char* p;
+    ~TmpFree() { cudaFree(p); }
+  } tmp_free{tmp};
   auto rq = [&](Lin& l, long row0, int rows) -> nmx_status_t {
     const size_t wpr = size_t(l.K) * bits / 32, ng = size_t(l.K) / gs;
-    return random_quantized(c, seed, sid++, stdv, rows, l.K, bits, gs, dt, l.w + row0 * wpr,
-                            static_cast<char*>(l.s) + row0 * ng * 2, static_cast<char*>(l.b) + row0 * ng * 2);
+    if (!l.dl)
+      return random_quantized(c, seed, sid++, stdv, rows, l.K, bits, gs, dt, l.w + row0 * wpr,
+                              static_cast<char*>(l.s) + row0 * ng * 2, static_cast<char*>(l.b) + row0 * ng * 2);
+    uint32_t* tw = reinterpret_cast<uint32_t*>(tmp);
+    char* ts = tmp + size_t(rows) * wpr * 4;
+    char* tb = ts + size_t(rows) * ng * 2;
+    NMX_TRY(random_quantized(c, seed, sid++, stdv, rows, l.K, bits, gs, dt, tw, ts, tb));
+    NMX_TRY(repack_to_records(c, tw, ts, tb, rows, l.K, row0, l.w, 7));
+    return cudaStreamSynchronize(c->stream) == cudaSuccess ? NMX_OK : NMX_ERR_CUDA;
   };
   NMX_TRY(random_fill(c, seed, sid++, stdv, 0.f, size_t(V) * H, dt, embed));
   NMX_TRY(fill_value(c, H, 1.0f, dt, final_norm));
@@ -262,8 +315,16 @@ nmx_status_t Model::init_random(uint64_t seed, float stdv) {
 nmx_status_t Model::resolve(const std::string& name, char** dst, size_t* bytes,
                             std::vector<int64_t>* shape, nmx_dtype_t* dtype) {
   const int H = cfg.hidden, F = cfg.ffn, V = cfg.vocab, gs = cfg.group_size, bits = cfg.bits;
+  rs_lin = nullptr;
   auto lin_part = [&](Lin& l, long row0, int rows, const std::string& part) -> nmx_status_t {
     const size_t wpr = size_t(l.K) * bits / 32, ng = size_t(l.K) / gs;
+    if (l.dl) {  // the part lives scattered inside decode records
+      rs_lin = &l;
+      rs_row0 = row0;
+      rs_rows = rows;
+      rs_mask = part == "weight" ? 1 : part == "scales" ? 2 : part == "biases" ? 4 : 0;
+      NMX_CHECK(rs_mask != 0, NMX_ERR_NOT_FOUND, "unknown tensor part: " + part);
+    }
     if (part == "weight") {
       *dst = reinterpret_cast<char*>(l.w + row0 * wpr);
       *bytes = size_t(rows) * wpr * 4;
@@ -353,7 +414,27 @@ nmx_status_t Model::load_tensor(const std::string& name, const void* host, nmx_d
     NMX_CHECK(shape[i] == exp[i], NMX_ERR_INVALID,
               "tensor " + name + ": dim " + std::to_string(i) + " is " + std::to_string(shape[i]) +
                   ", expected " + std::to_string(exp[i]));
-  NMX_CUDA_OK(cudaMemcpy(dst, host, bytes, cudaMemcpyHostToDevice));
+  if (rs_lin) {
+    Lin* l = rs_lin;
+    const long row0 = rs_row0;
+    const int rows = rs_rows, mask = rs_mask;
+    void* tmp = nullptr;
+    NMX_TRY(alloc_dev(&tmp, bytes));
+    // copy and repack are ordered on the model's stream (a pageable copy on
+    // another stream may still be in flight when the call returns)
+    cudaError_t e = cudaMemcpyAsync(tmp, host, bytes, cudaMemcpyHostToDevice, ctx->stream);
+    nmx_status_t st = NMX_OK;
+    if (e == cudaSuccess)
+      st = repack_to_records(ctx, mask == 1 ? static_cast<uint32_t*>(tmp) : nullptr, mask == 2 ? tmp : nullptr,
+                             mask == 4 ? tmp : nullptr, rows, l->K, row0, l->w, mask);
+    if (e == cudaSuccess && st == NMX_OK) e = cudaStreamSynchronize(ctx->stream);
+    cudaFree(tmp);
+    NMX_CUDA_OK(e);
+    NMX_TRY(st);
+  } else {
+    NMX_CUDA_OK(cudaMemcpyAsync(dst, host, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    NMX_CUDA_OK(cudaStreamSynchronize(ctx->stream));
+  }
   loaded_any = true;
   return NMX_OK;
 }
@@ -366,7 +447,23 @@ nmx_status_t Model::get_tensor(const std::string& name, void* host, size_t host_
   NMX_TRY(resolve(name, &src, &bytes, &exp, &edt));
   NMX_CHECK(host_bytes >= bytes, NMX_ERR_INVALID, "tensor " + name + ": host buffer too small");
   NMX_CUDA_OK(cudaStreamSynchronize(ctx->stream));
-  NMX_CUDA_OK(cudaMemcpy(host, src, bytes, cudaMemcpyDeviceToHost));
+  if (rs_lin) {
+    void* tmp = nullptr;
+    NMX_TRY(alloc_dev(&tmp, bytes));
+    const int mask = rs_mask;
+    nmx_status_t st = unpack_from_records(ctx, rs_lin->w, rs_rows, rs_lin->K, rs_row0,
+                                          mask == 1 ? static_cast<uint32_t*>(tmp) : nullptr,
+                                          mask == 2 ? tmp : nullptr, mask == 4 ? tmp : nullptr, mask);
+    cudaError_t e = cudaSuccess;
+    if (st == NMX_OK) e = cudaMemcpyAsync(host, tmp, bytes, cudaMemcpyDeviceToHost, ctx->stream);
+    if (st == NMX_OK && e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    cudaFree(tmp);
+    NMX_TRY(st);
+    NMX_CUDA_OK(e);
+    return NMX_OK;
+  }
+  NMX_CUDA_OK(cudaMemcpyAsync(host, src, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+  NMX_CUDA_OK(cudaStreamSynchronize(ctx->stream));
   return NMX_OK;
 }
 
@@ -404,6 +501,29 @@ KvPool::~KvPool() {
 
 // ------------------------------------------------------------------ forward
 
+nmx_status_t Model::linear(const Lin& l, const void* x, long ldx, const void* gamma, int M, int N_out,
+                           long pair_off_rows, const void* bias, void* y, long ldy, const void* res, long ldres,
+                           int epi, float* logits_f32, int* ids, int* next_tokens) {
+  if (l.dl) {
+    GemvDLArgs a;
+    a.x = x; a.ldx = ldx; a.gamma = gamma; a.eps = cfg.rms_eps; a.w = l.w;
+    a.N = N_out; a.K = l.K; a.M = M; a.pair_tiles = pair_off_rows / 16;
+    a.bias = bias; a.y = y; a.ldy = ldy; a.res = res; a.ldres = ldres;
+    a.logits_f32 = logits_f32; a.keys = dl_keys; a.done = dl_done; a.out_ids = ids; a.next_tokens = next_tokens;
+    a.partials = dl_partials; a.partials_cap = dl_partials_cap; a.counters = dl_counters;
+    a.ctas_per_sm = dl_ctas_per_sm;
+    return qgemv_dl(ctx, a, epi);
+  }
+  GemvArgs a;
+  a.weights_static = true;
+  a.x = x; a.ldx = ldx; a.gamma = gamma; a.eps = cfg.rms_eps;
+  a.w = l.w; a.s = l.s; a.b = l.b; a.N = N_out; a.K = l.K; a.M = M; a.pair_off = pair_off_rows;
+  a.bias = bias; a.y = y; a.ldy = ldy; a.res = res; a.ldres = ldres;
+  a.logits_f32 = logits_f32; a.part_val = am_val; a.part_idx = am_idx; a.counter = am_counter;
+  a.out_ids = ids; a.next_tokens = next_tokens;
+  return qgemv(ctx, a, cfg.bits, cfg.group_size, dt, epi);
+}
+
 nmx_status_t Model::run_layers_decode(KvPool* pool, int B) {
   Ctx* c = ctx;
   const nmx_model_cfg& cf = cfg;
@@ -413,11 +533,7 @@ nmx_status_t Model::run_layers_decode(KvPool* pool, int B) {
   NMX_TRY(embed_rows(c, embed, tok_ids, B, H, h));
   for (int l = 0; l < cf.n_layers; ++l) {
     LayerW& ly = layers[l];
-    GemvArgs q;
-    q.x = h; q.ldx = H; q.gamma = ly.attn_norm; q.eps = cf.rms_eps;
-    q.weights_static = true; q.w = ly.qkv.w; q.s = ly.qkv.s; q.b = ly.qkv.b; q.N = Nqkv; q.K = H; q.M = B;
-    q.bias = ly.qkv_bias; q.y = qkv; q.ldy = Nqkv;
-    NMX_TRY(qgemv(c, q, bits, gs, dt, EPI_STORE));
+    NMX_TRY(linear(ly.qkv, h, H, ly.attn_norm, B, Nqkv, 0, ly.qkv_bias, qkv, Nqkv, nullptr, 0, EPI_STORE));
 
     AttnArgs at;
     at.q = qkv; at.ldq = Nqkv;
@@ -429,21 +545,11 @@ nmx_status_t Model::run_layers_decode(KvPool* pool, int B) {
     at.splits = splits; at.scale = 1.0f / std::sqrt(float(cf.head_dim));
     NMX_TRY(paged_attention(c, at, true));
 
-    GemvArgs o;
-    o.weights_static = true; o.x = attn; o.ldx = Nq; o.w = ly.o.w; o.s = ly.o.s; o.b = ly.o.b; o.N = H; o.K = Nq; o.M = B;
-    o.y = h; o.ldy = H; o.res = h; o.ldres = H;
-    NMX_TRY(qgemv(c, o, bits, gs, dt, EPI_RESID));
+    NMX_TRY(linear(ly.o, attn, Nq, nullptr, B, H, 0, nullptr, h, H, h, H, EPI_RESID));
 
-    GemvArgs gu;
-    gu.x = h; gu.ldx = H; gu.gamma = ly.mlp_norm; gu.eps = cf.rms_eps;
-    gu.weights_static = true; gu.w = ly.gu.w; gu.s = ly.gu.s; gu.b = ly.gu.b; gu.N = F; gu.K = H; gu.M = B; gu.pair_off = F;
-    gu.y = act; gu.ldy = F;
-    NMX_TRY(qgemv(c, gu, bits, gs, dt, EPI_SILU));
+    NMX_TRY(linear(ly.gu, h, H, ly.mlp_norm, B, F, F, nullptr, act, F, nullptr, 0, EPI_SILU));
 
-    GemvArgs dn;
-    dn.weights_static = true; dn.x = act; dn.ldx = F; dn.w = ly.down.w; dn.s = ly.down.s; dn.b = ly.down.b; dn.N = H; dn.K = F;
-    dn.M = B; dn.y = h; dn.ldy = H; dn.res = h; dn.ldres = H;
-    NMX_TRY(qgemv(c, dn, bits, gs, dt, EPI_RESID));
+    NMX_TRY(linear(ly.down, act, F, nullptr, B, H, 0, nullptr, h, H, h, H, EPI_RESID));
   }
   return NMX_OK;
 }
@@ -455,11 +561,7 @@ nmx_status_t Model::run_layers_prefill(KvPool* pool, int T) {
   NMX_TRY(embed_rows(c, embed, tok_ids, T, H, h));
   for (int l = 0; l < cf.n_layers; ++l) {
     LayerW& ly = layers[l];
-    GemvArgs q;
-    q.x = h; q.ldx = H; q.gamma = ly.attn_norm; q.eps = cf.rms_eps;
-    q.weights_static = true; q.w = ly.qkv.w; q.s = ly.qkv.s; q.b = ly.qkv.b; q.N = Nqkv; q.K = H; q.M = T;
-    q.bias = ly.qkv_bias; q.y = qkv; q.ldy = Nqkv;
-    NMX_TRY(qgemv(c, q, bits, gs, dt, EPI_STORE));
+    NMX_TRY(linear(ly.qkv, h, H, ly.attn_norm, T, Nqkv, 0, ly.qkv_bias, qkv, Nqkv, nullptr, 0, EPI_STORE));
     NMX_TRY(rope_append(c, qkv, Nqkv, T, cf.n_heads, cf.n_kv_heads, cf.head_dim, tok_seq, tok_pos,
                         block_tables, kBlockCap, kBT, pool->k_layer(l), pool->v_layer(l), inv_freq,
                         q_roped, Nq));
@@ -473,21 +575,11 @@ nmx_status_t Model::run_layers_prefill(KvPool* pool, int T) {
     at.splits = 1; at.scale = 1.0f / std::sqrt(float(cf.head_dim));
     NMX_TRY(paged_attention(c, at, false));
 
-    GemvArgs o;
-    o.weights_static = true; o.x = attn; o.ldx = Nq; o.w = ly.o.w; o.s = ly.o.s; o.b = ly.o.b; o.N = H; o.K = Nq; o.M = T;
-    o.y = h; o.ldy = H; o.res = h; o.ldres = H;
-    NMX_TRY(qgemv(c, o, bits, gs, dt, EPI_RESID));
+    NMX_TRY(linear(ly.o, attn, Nq, nullptr, T, H, 0, nullptr, h, H, h, H, EPI_RESID));
 
-    GemvArgs gu;
-    gu.x = h; gu.ldx = H; gu.gamma = ly.mlp_norm; gu.eps = cf.rms_eps;
-    gu.weights_static = true; gu.w = ly.gu.w; gu.s = ly.gu.s; gu.b = ly.gu.b; gu.N = F; gu.K = H; gu.M = T; gu.pair_off = F;
-    gu.y = act; gu.ldy = F;
-    NMX_TRY(qgemv(c, gu, bits, gs, dt, EPI_SILU));
+    NMX_TRY(linear(ly.gu, h, H, ly.mlp_norm, T, F, F, nullptr, act, F, nullptr, 0, EPI_SILU));
 
-    GemvArgs dn;
-    dn.weights_static = true; dn.x = act; dn.ldx = F; dn.w = ly.down.w; dn.s = ly.down.s; dn.b = ly.down.b; dn.N = H; dn.K = F;
-    dn.M = T; dn.y = h; dn.ldy = H; dn.res = h; dn.ldres = H;
-    NMX_TRY(qgemv(c, dn, bits, gs, dt, EPI_RESID));
+    NMX_TRY(linear(ly.down, act, F, nullptr, T, H, 0, nullptr, h, H, h, H, EPI_RESID));
   }
   return NMX_OK;
 }
@@ -497,18 +589,12 @@ nmx_status_t Model::run_layers_prefill(KvPool* pool, int T) {
 nmx_status_t Model::run_head(const void* x, int rows, bool want_logits, int* next_tokens) {
   Ctx* c = ctx;
   const int H = cfg.hidden, V = cfg.vocab;
-  for (int r0 = 0; r0 < rows; r0 += 32) {
-    const int rc = std::min(32, rows - r0);
-    GemvArgs hd;
-    hd.x = static_cast<const char*>(x) + size_t(r0) * H * 2;
-    hd.ldx = H; hd.gamma = final_norm; hd.eps = cfg.rms_eps;
-    hd.weights_static = true; hd.w = lm.w; hd.s = lm.s; hd.b = lm.b; hd.N = V; hd.K = H; hd.M = rc;
-    hd.y = nullptr; hd.ldy = V;
-    hd.logits_f32 = want_logits ? logits_f32 + size_t(r0) * V : nullptr;
-    hd.part_val = am_val; hd.part_idx = am_idx; hd.counter = am_counter;
-    hd.out_ids = out_ids + r0;
-    hd.next_tokens = next_tokens ? next_tokens + r0 : nullptr;
-    NMX_TRY(qgemv(c, hd, cfg.bits, cfg.group_size, dt, EPI_ARGMAX));
+  const int chunk = lm.dl ? std::min(32, qgemv_dl_max_m(H, EPI_ARGMAX)) : 32;
+  for (int r0 = 0; r0 < rows; r0 += chunk) {
+    const int rc = std::min(chunk, rows - r0);
+    NMX_TRY(linear(lm, static_cast<const char*>(x) + size_t(r0) * H * 2, H, final_norm, rc, V, 0, nullptr, nullptr,
+                   V, nullptr, 0, EPI_ARGMAX, want_logits ? logits_f32 + size_t(r0) * V : nullptr, out_ids + r0,
+                   next_tokens ? next_tokens + r0 : nullptr));
   }
   return NMX_OK;
 }

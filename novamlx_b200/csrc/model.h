@@ -11,10 +11,12 @@
 namespace nmx {
 
 struct Lin {
-  uint32_t* w = nullptr;  // packed [N, K*bits/32]
-  void* s = nullptr;      // [N, K/gs]
+  uint32_t* w = nullptr;  // packed [N, K*bits/32], or the decode records when dl
+  void* s = nullptr;      // [N, K/gs] (MLX layout only)
   void* b = nullptr;
   int N = 0, K = 0;
+  bool dl = false;        // stored as decode records (see qgemv_dl.cu)
+  size_t bytes = 0;       // words + scales + biases
 };
 
 struct LayerW {
@@ -67,6 +69,11 @@ struct Model {
   size_t h2d_bytes_last = 0;
   std::map<std::pair<int, const void*>, GraphEntry> graphs;
 
+  // set by resolve() when the named part lives inside decode records
+  Lin* rs_lin = nullptr;
+  long rs_row0 = 0;
+  int rs_rows = 0, rs_mask = 0;
+
   static nmx_status_t create(Ctx* c, const nmx_model_cfg& cfg, Model** out);
   ~Model();
   nmx_status_t init_random(uint64_t seed, float stdv);
@@ -76,6 +83,18 @@ struct Model {
                            int ndim);
   nmx_status_t get_tensor(const std::string& name, void* host, size_t host_bytes);
 
+  // partial-sum scratch and counters of the decode-record GEMV
+  float* dl_partials = nullptr;
+  size_t dl_partials_cap = 0;
+  unsigned* dl_counters = nullptr;
+  unsigned long long* dl_keys = nullptr;
+  unsigned* dl_done = nullptr;
+  int dl_ctas_per_sm = 2;
+
+  // y = epilogue(norm?(x) · W^T) through whichever GEMV the layout calls for
+  nmx_status_t linear(const Lin& l, const void* x, long ldx, const void* gamma, int M, int N_out,
+                      long pair_off_rows, const void* bias, void* y, long ldy, const void* res, long ldres,
+                      int epi, float* logits_f32 = nullptr, int* ids = nullptr, int* next_tokens = nullptr);
   nmx_status_t run_layers_decode(KvPool* pool, int B);
   nmx_status_t run_layers_prefill(KvPool* pool, int T);
   nmx_status_t run_head(const void* x, int rows, bool want_logits, int* next_tokens);

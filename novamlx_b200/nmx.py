@@ -43,6 +43,7 @@ def _load() -> C.CDLL:
 
 
 lib = _load()
+_is_finalizing = sys.is_finalizing  # module globals may be gone when __del__ runs at exit
 
 _vp, _i, _u64, _f, _sz = C.c_void_p, C.c_int, C.c_uint64, C.c_float, C.c_size_t
 _ip = C.POINTER(C.c_int32)
@@ -78,6 +79,8 @@ _proto("nmx_ctx_stream", _vp, _vp)
 _proto("nmx_ctx_synchronize", _i, _vp)
 _proto("nmx_ctx_kernel_launches", _u64, _vp)
 _proto("nmx_op_qmatmul", _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp)
+_proto("nmx_op_pack_records", _i, _vp, _vp, _vp, _vp, _i, _i, _vp)
+_proto("nmx_op_qmatmul_records", _i, _vp, _vp, _vp, _i, _i, _i, _vp)
 _proto("nmx_op_quantize", _i, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp)
 _proto("nmx_op_dequantize", _i, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp)
 _proto("nmx_op_rmsnorm", _i, _vp, _vp, _vp, _i, _i, _f, _i, _vp)
@@ -206,7 +209,7 @@ class Context:
             self.h = None
 
     def __del__(self):
-        if sys.is_finalizing():
+        if _is_finalizing():
             return  # the process is exiting; the driver reclaims device memory
         try:
             self.close()
@@ -224,6 +227,24 @@ class Context:
             out = torch.empty((M, N), dtype=x.dtype, device=x.device)
         check(self._op(lambda: lib.nmx_op_qmatmul(self.h, _ptr(x), _ptr(w), _ptr(scales), _ptr(biases), M, N, K,
                                                   bits, group_size, 1 if transpose else 0, _dt_of(x), _ptr(out))))
+        return out
+
+    def pack_records(self, wq, scales, biases):
+        """Decode-record copy of a 4-bit g64 f16 linear (uint8 tensor of N*K*9/16 bytes)."""
+        import torch
+        N = wq.shape[0]
+        K = wq.shape[1] * 8
+        rec = torch.empty((N * K * 9 // 16,), dtype=torch.uint8, device=wq.device)
+        check(self._op(lambda: lib.nmx_op_pack_records(self.h, _ptr(wq), _ptr(scales), _ptr(biases), N, K,
+                                                       _ptr(rec))))
+        return rec
+
+    def quantized_matmul_records(self, x, records, N: int, out=None):
+        import torch
+        M, K = x.shape
+        if out is None:
+            out = torch.empty((M, N), dtype=x.dtype, device=x.device)
+        check(self._op(lambda: lib.nmx_op_qmatmul_records(self.h, _ptr(x), _ptr(records), M, N, K, _ptr(out))))
         return out
 
     def quantize(self, w, group_size: int = 64, bits: int = 4, scale_dtype=None):
@@ -375,7 +396,7 @@ class Model:
             self.h = None
 
     def __del__(self):
-        if sys.is_finalizing():
+        if _is_finalizing():
             return  # the process is exiting; the driver reclaims device memory
         try:
             self.close()
@@ -490,7 +511,7 @@ class KVPool:
             self.h = None
 
     def __del__(self):
-        if sys.is_finalizing():
+        if _is_finalizing():
             return  # the process is exiting; the driver reclaims device memory
         try:
             self.close()
@@ -532,7 +553,7 @@ class PagedBlockPool:
         self.block_size = block_size
 
     def __del__(self):
-        if getattr(self, "h", None) and not sys.is_finalizing():
+        if getattr(self, "h", None) and not _is_finalizing():
             lib.nmx_block_pool_destroy(self.h)
             self.h = None
 

@@ -194,3 +194,32 @@ def test_random_init_model_runs(ctx):
     first = m.forward(pool, [dict(tokens=prompt, start_pos=0, block_table=np.arange(16))])
     ids = m.decode_greedy(pool, first, [100], np.arange(16)[None], 20)
     assert ids.shape == (20, 1) and np.all((ids >= 0) & (ids < cfg.vocab))
+
+
+def test_wide_layer_matches_oracle(ctx):
+    """One layer at the 8B widths (hidden 4096, 32/8 heads, ffn 14336) and a
+    32K vocabulary: tile groups split over several warps (stream-K fixup)."""
+    from novamlx_b200 import nmx
+    d = dict(vocab=32768, hidden=4096, n_layers=1, n_heads=32, n_kv_heads=8, head_dim=128, ffn=14336,
+             rope_theta=500000.0, rms_eps=1e-5)
+    ocfg = O.TinyCfg(**d)
+    tensors = O.random_tensors(ocfg, seed=2, std=0.02)
+    om = O.OracleModel(ocfg, tensors)
+    m = nmx.Model(ctx, nmx.ModelConfig(**d, max_batch=4, max_tokens=64))
+    for k, v in tensors.items():
+        m.load_tensor(k, v.view(np.float16) if v.dtype == np.uint16 else v)
+    pool = nmx.KVPool(m, 16)
+    rng = np.random.default_rng(4)
+    prompt = rng.integers(0, d["vocab"], 21)
+    table = np.array([7, 3, 12, 0], np.int32)
+    got = m.forward(pool, [dict(tokens=prompt, start_pos=0, block_table=table)], nmx.OUT_LOGITS_LAST)
+    cache = om.new_cache(64)
+    check_logits(got, om.forward(cache, prompt, 0))
+    pos = len(prompt)
+    for _ in range(3):
+        tok = int(rng.integers(0, d["vocab"]))
+        g = m.forward(pool, [dict(tokens=[tok], start_pos=pos, block_table=table)], nmx.OUT_LOGITS_LAST)
+        check_logits(g, om.forward(cache, [tok], pos))
+        ids = m.forward(pool, [dict(tokens=[tok], start_pos=pos, block_table=table)], nmx.OUT_ARGMAX_LAST)
+        assert ids[0] == int(np.argmax(g[0]))
+        pos += 1

@@ -109,6 +109,23 @@ def test_qmatmul_shapes(env, M, N, K, bits, gs):
     assert O.max_rel_err(got, ref) <= 2e-3, (M, N, K, bits, gs)
 
 
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8, 9, 13, 32])
+@pytest.mark.parametrize("N,K", [(4096, 4096), (256, 512), (4096, 14336), (768, 512)])
+def test_qmatmul_records(env, M, N, K):
+    """The decode-record GEMV (the model's layout) equals the oracle."""
+    torch, nmx, ctx = env
+    rng = np.random.default_rng(M * 31 + N + K)
+    w = rng.standard_normal((N, K), dtype=np.float32) * 0.02
+    wq, s, b = O.quantize(w, 4, 64)
+    x = O.f32_to_f16bits(rng.standard_normal((M, K), dtype=np.float32))
+    ref = O.f16bits_to_f32(O.qmatmul(x, wq, s, b, 4, 64))
+    rec = ctx.pack_records(dev(torch, wq.view(np.int32)), u16(torch, s), u16(torch, b))
+    y = ctx.quantized_matmul_records(u16(torch, x), rec, N)
+    got = O.f16bits_to_f32(host16(y))
+    for m in range(M):
+        assert O.max_rel_err(got[m], ref[m]) <= 2e-3, (m, M)
+
+
 def test_qmatmul_bf16(env):
     torch, nmx, ctx = env
     rng = np.random.default_rng(4)
