@@ -43,7 +43,6 @@ def _load() -> C.CDLL:
 
 
 lib = _load()
-_is_finalizing = sys.is_finalizing  # module globals may be gone when __del__ runs at exit
 
 _vp, _i, _u64, _f, _sz = C.c_void_p, C.c_int, C.c_uint64, C.c_float, C.c_size_t
 _ip = C.POINTER(C.c_int32)
@@ -208,8 +207,8 @@ class Context:
             lib.nmx_ctx_destroy(self.h)
             self.h = None
 
-    def __del__(self):
-        if _is_finalizing():
+    def __del__(self, _finalizing=sys.is_finalizing):
+        if _finalizing():
             return  # the process is exiting; the driver reclaims device memory
         try:
             self.close()
@@ -395,8 +394,8 @@ class Model:
             lib.nmx_model_destroy(self.h)
             self.h = None
 
-    def __del__(self):
-        if _is_finalizing():
+    def __del__(self, _finalizing=sys.is_finalizing):
+        if _finalizing():
             return  # the process is exiting; the driver reclaims device memory
         try:
             self.close()
@@ -510,8 +509,8 @@ class KVPool:
             lib.nmx_kv_pool_destroy(self.h)
             self.h = None
 
-    def __del__(self):
-        if _is_finalizing():
+    def __del__(self, _finalizing=sys.is_finalizing):
+        if _finalizing():
             return  # the process is exiting; the driver reclaims device memory
         try:
             self.close()
@@ -552,8 +551,8 @@ class PagedBlockPool:
         self.h = h
         self.block_size = block_size
 
-    def __del__(self):
-        if getattr(self, "h", None) and not _is_finalizing():
+    def __del__(self, _finalizing=sys.is_finalizing):
+        if getattr(self, "h", None) and not _finalizing():
             lib.nmx_block_pool_destroy(self.h)
             self.h = None
 
