@@ -174,6 +174,25 @@ NMX_API nmx_status_t nmx_op_attn_paged_decode(nmx_ctx_t ctx, const void* q, cons
                                               int D, int block_tokens, int max_blocks,
                                               float scale, void* out);
 
+/* The same decode attention as nmx_op_attn_paged_decode, for callers that
+ * cannot allocate device memory (a host that reserves its whole device
+ * budget up front and admits work against it, or one that cannot afford the
+ * device synchronisation cudaMalloc/cudaFree may cause). Its scratch (split
+ * partial sums, tickets, row descriptors) lives in a fixed 8 MiB array inside
+ * the library, held on every GPU that loads it until exit; it never
+ * allocates. The first call on a device looks up that array's address with
+ * the device current; make it before any stream capture. Calls share the
+ * array: calls that overlap on the GPU race. It uses fewer key splits than
+ * nmx_op_attn_paged_decode when they would not fit (results can then differ
+ * in the last bits) and returns NMX_ERR_UNSUPPORTED when even one split does
+ * not fit. No counterpart in the reference. */
+NMX_API nmx_status_t nmx_op_attn_paged_decode_noalloc(nmx_ctx_t ctx, const void* q,
+                                                      const void* k_cache, const void* v_cache,
+                                                      const int32_t* block_tables,
+                                                      const int32_t* seq_lens, int B, int Hq,
+                                                      int Hkv, int D, int block_tokens,
+                                                      int max_blocks, float scale, void* out);
+
 /* ------------------------------------------------------------------------ */
 /* Model level                                                               */
 /* ------------------------------------------------------------------------ */

@@ -88,6 +88,7 @@ _proto("nmx_op_penalized_argmax", _i, _vp, _vp, _i, _i, _i, _vp, _vp, _i, _f, _v
 _proto("nmx_op_attn_quantized_decode", _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f,
        _i, _i, _i, _i, _vp)
 _proto("nmx_op_attn_paged_decode", _i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp)
+_proto("nmx_op_attn_paged_decode_noalloc", _i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _f, _vp)
 _proto("nmx_model_create", _i, _vp, C.POINTER(ModelCfg), C.POINTER(_vp))
 _proto("nmx_model_destroy", _i, _vp)
 _proto("nmx_model_init_random", _i, _vp, _u64, _f)
@@ -315,6 +316,22 @@ class Context:
         check(self._op(lambda: lib.nmx_op_attn_paged_decode(self.h, _ptr(q), kp, vp, _ptr(block_tables),
                                                             _ptr(seq_lens), B, Hq, n_kv_heads, D, block_tokens,
                                                             block_tables.shape[1], scale, _ptr(out))))
+        return out
+
+
+    def paged_decode_attention_noalloc(self, q, k_cache, v_cache, block_tables, seq_lens, n_kv_heads: int,
+                                       scale: float, block_tokens: int = 16, out=None):
+        """paged_decode_attention through the entry point that never allocates
+        device memory (its scratch is a fixed array inside the library)."""
+        import torch
+        B, Hq, D = q.shape
+        if out is None:
+            out = torch.empty_like(q)
+        kp = k_cache if isinstance(k_cache, int) else _ptr(k_cache)
+        vp = v_cache if isinstance(v_cache, int) else _ptr(v_cache)
+        check(self._op(lambda: lib.nmx_op_attn_paged_decode_noalloc(
+            self.h, _ptr(q), kp, vp, _ptr(block_tables), _ptr(seq_lens), B, Hq, n_kv_heads, D, block_tokens,
+            block_tables.shape[1], scale, _ptr(out))))
         return out
 
 
