@@ -23,8 +23,6 @@ namespace nmx {
 
 namespace {
 
-constexpr int kAttnThreads = 128;
-constexpr int kAttnWarps = 4;
 constexpr int kMaxRep = 8;
 
 __device__ __forceinline__ void rope_pair(float a, float b, float ang, float& ra, float& rb) {
@@ -32,207 +30,6 @@ __device__ __forceinline__ void rope_pair(float a, float b, float ang, float& ra
   sincosf(ang, &sn, &cs);
   ra = a * cs - b * sn;
   rb = b * cs + a * sn;
-}
-
-template <int D, bool FUSED>
-__global__ void __launch_bounds__(kAttnThreads) paged_attn_kernel(AttnArgs a) {
-  constexpr int BT = 16;
-  constexpr int KST = D / 2 + 2;  // K row stride in 32-bit words (bank-conflict free)
-  constexpr int DPL = D / 32;     // dims per lane in P·V
-  constexpr int NH = kMaxRep / kAttnWarps;
-  __shared__ float q_s[kMaxRep][D];
-  __shared__ __align__(16) uint32_t k_s[BT * KST];
-  __shared__ __align__(16) uint32_t v_s[BT * KST];
-  __shared__ float p_s[kMaxRep][BT];
-  __shared__ int s_last;
-
-  const int split = blockIdx.x, h = blockIdx.y, row = blockIdx.z;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int Hq = a.Hq, Hkv = a.Hkv, rep = Hq / Hkv, S = gridDim.x;
-
-  grid_wait();
-  const int seq = a.tok_seq[row];
-  const int pos = a.tok_pos[row];
-  const int L = pos + 1;
-  const int nblk = (L + BT - 1) / BT;
-  const int bps = (nblk + S - 1) / S;
-  const int b0 = split * bps;
-  const int b1 = min(nblk, b0 + bps);
-  const int* bt = a.block_tables + long(seq) * a.max_blocks;
-  half* Kc = reinterpret_cast<half*>(a.k_cache);
-  half* Vc = reinterpret_cast<half*>(a.v_cache);
-  const half* Q = reinterpret_cast<const half*>(a.q) + long(row) * a.ldq;
-
-  // ---- q (optionally roped), pre-scaled, fp32 in shared memory
-  if (FUSED) {
-    for (int i = tid; i < rep * (D / 2); i += kAttnThreads) {
-      const int hi = i / (D / 2), d = i % (D / 2);
-      const int hq = h * rep + hi;
-      const float x0 = __half2float(Q[hq * D + d]), x1 = __half2float(Q[hq * D + d + D / 2]);
-      float r0, r1;
-      rope_pair(x0, x1, float(pos) * a.inv_freq[d], r0, r1);
-      q_s[hi][d] = rnd<half>(r0) * a.scale;
-      q_s[hi][d + D / 2] = rnd<half>(r1) * a.scale;
-    }
-    // append this row's k/v when its position falls in this split
-    if (pos >= b0 * BT && pos < b1 * BT) {
-      const long slot = (long(bt[pos / BT]) * Hkv + h) * BT + pos % BT;
-      const half* kr = Q + (Hq + h) * D;
-      const half* vr = Q + (Hq + Hkv + h) * D;
-      for (int d = tid; d < D / 2; d += kAttnThreads) {
-        float r0, r1;
-        rope_pair(__half2float(kr[d]), __half2float(kr[d + D / 2]), float(pos) * a.inv_freq[d], r0, r1);
-        Kc[slot * D + d] = __float2half_rn(r0);
-        Kc[slot * D + d + D / 2] = __float2half_rn(r1);
-      }
-      for (int d = tid; d < D; d += kAttnThreads) Vc[slot * D + d] = vr[d];
-    }
-  } else {
-    for (int i = tid; i < rep * D; i += kAttnThreads) {
-      const int hi = i / D, d = i % D;
-      q_s[hi][d] = __half2float(Q[(h * rep + hi) * D + d]) * a.scale;
-    }
-  }
-  __syncthreads();
-
-  float m_run[NH], l_run[NH], o[NH][DPL];
-#pragma unroll
-  for (int j = 0; j < NH; ++j) {
-    m_run[j] = -INFINITY;
-    l_run[j] = 0.f;
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) o[j][e] = 0.f;
-  }
-
-  const int tok = lane >> 1, hv = lane & 1;
-  for (int b = b0; b < b1; ++b) {
-    const long base = (long(bt[b]) * Hkv + h) * BT * D;  // in halves
-    // stage K and V blocks (BT*D halves each) with 16-byte loads
-    {
-      const uint4* ks = reinterpret_cast<const uint4*>(Kc + base);
-      const uint4* vs = reinterpret_cast<const uint4*>(Vc + base);
-      constexpr int NV = BT * D / 8;
-      for (int i = tid; i < NV; i += kAttnThreads) {
-        const int r = i / (D / 8), c = i % (D / 8);
-        const uint4 kv = ks[i], vv = vs[i];
-        uint32_t* kd = k_s + r * KST + c * 4;
-        uint32_t* vd = v_s + r * KST + c * 4;
-        kd[0] = kv.x; kd[1] = kv.y; kd[2] = kv.z; kd[3] = kv.w;
-        vd[0] = vv.x; vd[1] = vv.y; vd[2] = vv.z; vd[3] = vv.w;
-      }
-    }
-    __syncthreads();
-    const bool valid = (b * BT + tok) <= pos;
-#pragma unroll
-    for (int j = 0; j < NH; ++j) {
-      const int hi = warp + j * kAttnWarps;
-      if (hi < rep) {
-        // score of token `tok`, half of the words per lane (interleaved)
-        float sc = 0.f;
-#pragma unroll 8
-        for (int w = 0; w < D / 4; ++w) {
-          const int word = 2 * w + hv;
-          const __half2 kk = *reinterpret_cast<const __half2*>(k_s + tok * KST + word);
-          const float2 kf = __half22float2(kk);
-          sc = fmaf(q_s[hi][2 * word], kf.x, fmaf(q_s[hi][2 * word + 1], kf.y, sc));
-        }
-        sc += __shfl_xor_sync(0xffffffffu, sc, 1);
-        sc = valid ? sc : -INFINITY;
-        float mb = sc;
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, off));
-        const float m_new = fmaxf(m_run[j], mb);
-        const float f = expf(m_run[j] - m_new);
-        const float p = valid ? expf(sc - m_new) : 0.f;
-        float ps = hv == 0 ? p : 0.f;
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
-        l_run[j] = l_run[j] * f + ps;
-        m_run[j] = m_new;
-        if (hv == 0) p_s[hi][tok] = p;
-        __syncwarp();
-#pragma unroll
-        for (int e = 0; e < DPL; ++e) o[j][e] *= f;
-#pragma unroll
-        for (int t2 = 0; t2 < BT; ++t2) {
-          const float pt = p_s[hi][t2];
-#pragma unroll
-          for (int e = 0; e < DPL; e += 2) {
-            const int word = lane + (e / 2) * 32;
-            const float2 vf = __half22float2(*reinterpret_cast<const __half2*>(v_s + t2 * KST + word));
-            o[j][e] = fmaf(pt, vf.x, o[j][e]);
-            o[j][e + 1] = fmaf(pt, vf.y, o[j][e + 1]);
-          }
-        }
-        __syncwarp();
-      }
-    }
-    __syncthreads();
-  }
-  grid_launch_dependents();
-
-  half* Out = reinterpret_cast<half*>(a.out) + long(row) * Hq * D;
-  if (S == 1) {
-#pragma unroll
-    for (int j = 0; j < NH; ++j) {
-      const int hi = warp + j * kAttnWarps;
-      if (hi < rep) {
-        const int hq = h * rep + hi;
-        const float inv = l_run[j] > 0.f ? 1.0f / l_run[j] : 0.f;
-#pragma unroll
-        for (int e = 0; e < DPL; e += 2) {
-          const int d = 2 * (lane + (e / 2) * 32);
-          *reinterpret_cast<__half2*>(Out + hq * D + d) =
-              __floats2half2_rn(o[j][e] * inv, o[j][e + 1] * inv);
-        }
-      }
-    }
-    return;
-  }
-
-  // ---- split-KV: publish partials; the last CTA of (row, h) combines
-#pragma unroll
-  for (int j = 0; j < NH; ++j) {
-    const int hi = warp + j * kAttnWarps;
-    if (hi < rep) {
-      const int hq = h * rep + hi;
-      const long pb = (long(row) * Hq + hq) * S + split;
-#pragma unroll
-      for (int e = 0; e < DPL; e += 2) {
-        const int d = 2 * (lane + (e / 2) * 32);
-        *reinterpret_cast<float2*>(a.part_o + pb * D + d) = make_float2(o[j][e], o[j][e + 1]);
-      }
-      if (lane == 0) *reinterpret_cast<float2*>(a.part_ml + pb * 2) = make_float2(m_run[j], l_run[j]);
-    }
-  }
-  __threadfence();
-  __syncthreads();
-  unsigned* ctr = a.counters + long(row) * Hkv + h;
-  if (tid == 0) s_last = (atomicAdd(ctr, 1u) == unsigned(S - 1)) ? 1 : 0;
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  for (int i = tid; i < rep * D; i += kAttnThreads) {
-    const int hi = i / D, d = i % D;
-    const int hq = h * rep + hi;
-    const long pb = (long(row) * Hq + hq) * S;
-    float mx = -INFINITY;
-    for (int s2 = 0; s2 < S; ++s2) {
-      const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml + (pb + s2) * 2));
-      if (ml.y > 0.f) mx = fmaxf(mx, ml.x);
-    }
-    float num = 0.f, den = 0.f;
-    for (int s2 = 0; s2 < S; ++s2) {
-      const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml + (pb + s2) * 2));
-      if (ml.y > 0.f) {
-        const float w = expf(ml.x - mx);
-        den = fmaf(ml.y, w, den);
-        num = fmaf(__ldcg(a.part_o + (pb + s2) * D + d), w, num);
-      }
-    }
-    Out[hq * D + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
-  }
-  if (tid == 0) *ctr = 0u;
 }
 
 template <int D>
@@ -351,15 +148,7 @@ nmx_status_t paged_attention(Ctx* c, const AttnArgs& a, bool fused) {
             "paged attention: q heads per kv head must be <= 8");
   NMX_CHECK(a.splits >= 1, NMX_ERR_INVALID, "paged attention: splits >= 1");
   if (a.T == 0) return NMX_OK;
-  dim3 grid(a.splits, a.Hkv, a.T);
-  if (a.D == 128) {
-    return fused ? launch(c, paged_attn_kernel<128, true>, grid, dim3(kAttnThreads), 0, a)
-                 : launch(c, paged_attn_kernel<128, false>, grid, dim3(kAttnThreads), 0, a);
-  } else if (a.D == 64) {
-    return fused ? launch(c, paged_attn_kernel<64, true>, grid, dim3(kAttnThreads), 0, a)
-                 : launch(c, paged_attn_kernel<64, false>, grid, dim3(kAttnThreads), 0, a);
-  }
-  NMX_CHECK(false, NMX_ERR_UNSUPPORTED, "paged attention: head_dim must be 64 or 128");
+  return paged_attention_mma(c, a, fused);
 }
 
 nmx_status_t rope_append(Ctx* c, void* qkv, long ldq, int T, int Hq, int Hkv, int D,

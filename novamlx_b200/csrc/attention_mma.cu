@@ -1,0 +1,355 @@
+// Paged decode attention on the tensor cores (one query row per sequence).
+//
+// A CTA owns (query row, kv head, key split) and serves all q heads of the
+// GQA group (rep <= 8 rows of a 16-row MMA tile). Its four warps take the
+// split's 16-token blocks round-robin; each warp streams K and V blocks
+// through its own two-stage cp.async ring into XOR-swizzled shared tiles
+// (16 B chunk c of row r at chunk c ^ (r & 7): conflict-free ldmatrix), and
+// per block runs S = Q·Kᵀ (mma.sync m16n8k16, f16 in, f32 out), an online
+// softmax in the log2 domain on the accumulator fragments, and O += P·V with
+// P taken straight from the S fragments and V fed by ldmatrix.trans. The
+// warps' states merge through shared memory; splits are merged by the last
+// CTA of (row, kv head) to finish (atomic ticket, no waiting), with the
+// per-split weights computed once and the partial rows read in parallel.
+//
+// In decode (FUSED) the CTA also applies RoPE to q and, when its split holds
+// the new position, writes the new token's roped k and its v to the page
+// before any warp reads it.
+#include <map>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace nmx {
+
+namespace {
+
+constexpr int kAW = 4;        // warps per CTA
+constexpr int kAStages = 2;   // cp.async stages per warp
+constexpr int kMaxRepA = 8;   // q heads per kv head
+constexpr int kMaxSplitsA = 32;
+
+__device__ __forceinline__ void cp_async16a(void* smem_dst, const void* gsrc) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t* r, const void* p) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(s));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t* r, const void* p) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(s));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t* r, const void* p) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];\n" : "=r"(r[0]), "=r"(r[1]) : "r"(s));
+}
+
+__device__ __forceinline__ void mma_f16(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// byte offset of (row, 16-byte chunk) in a swizzled [16][D] f16 tile
+template <int D>
+__device__ __forceinline__ int swz(int row, int chunk) {
+  return row * (D * 2) + ((chunk ^ (row & 7)) << 4);
+}
+
+__device__ __forceinline__ void rope2(float a, float b, float ang, float& ra, float& rb) {
+  float sn, cs;
+  sincosf(ang, &sn, &cs);
+  ra = a * cs - b * sn;
+  rb = b * cs + a * sn;
+}
+
+template <int D, bool FUSED>
+__global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) {
+  constexpr int BT = 16;
+  constexpr int CH = D / 8;          // 16-byte chunks per row
+  constexpr int TILE = BT * D * 2;   // bytes of one K (or V) block tile
+  constexpr int KSTEPS = D / 16;
+  constexpr int NT = D / 8;
+  constexpr float kLog2e = 1.4426950408889634f;
+  extern __shared__ __align__(128) unsigned char sm[];
+  unsigned char* q_sm = sm;
+  unsigned char* ring_all = sm + TILE;
+  __shared__ float s_m[kAW][kMaxRepA], s_l[kAW][kMaxRepA];
+  __shared__ float s_w[kMaxRepA][kMaxSplitsA];
+  __shared__ float s_cm[kMaxRepA * kMaxSplitsA], s_cl[kMaxRepA * kMaxSplitsA];
+  __shared__ int s_last;
+
+  const int split = blockIdx.x, h = blockIdx.y, row = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int Hq = a.Hq, Hkv = a.Hkv, rep = Hq / Hkv, S = gridDim.x;
+
+  grid_wait();
+  const int seq = a.tok_seq[row];
+  const int pos = a.tok_pos[row];
+  const int nblk = (pos + 1 + BT - 1) / BT;
+  const int bps = (nblk + S - 1) / S;
+  const int b0 = split * bps;
+  const int b1 = min(nblk, b0 + bps);
+  const int* bt = a.block_tables + long(seq) * a.max_blocks;
+  half* Kc = reinterpret_cast<half*>(a.k_cache);
+  half* Vc = reinterpret_cast<half*>(a.v_cache);
+  const half* Q = reinterpret_cast<const half*>(a.q) + long(row) * a.ldq;
+
+  // ---- q tile: rows < rep hold the (roped) q heads, rows >= rep are zero
+  for (int i = tid; i < (BT - rep) * CH; i += kAW * 32) {
+    const int r = rep + i / CH, c = i % CH;
+    *reinterpret_cast<uint4*>(q_sm + swz<D>(r, c)) = make_uint4(0, 0, 0, 0);
+  }
+  if (FUSED) {
+    for (int i = tid; i < rep * (D / 2); i += kAW * 32) {
+      const int hi = i / (D / 2), d = i % (D / 2);
+      const int hq = h * rep + hi;
+      float r0, r1;
+      rope2(__half2float(Q[hq * D + d]), __half2float(Q[hq * D + d + D / 2]), float(pos) * a.inv_freq[d], r0, r1);
+      half* q0 = reinterpret_cast<half*>(q_sm + swz<D>(hi, d / 8)) + (d % 8);
+      half* q1 = reinterpret_cast<half*>(q_sm + swz<D>(hi, (d + D / 2) / 8)) + (d % 8);
+      *q0 = __float2half_rn(r0);
+      *q1 = __float2half_rn(r1);
+    }
+    if (pos >= b0 * BT && pos < b1 * BT) {
+      const long slot = (long(bt[pos / BT]) * Hkv + h) * BT + pos % BT;
+      const half* kr = Q + (Hq + h) * D;
+      const half* vr = Q + (Hq + Hkv + h) * D;
+      for (int d = tid; d < D / 2; d += kAW * 32) {
+        float r0, r1;
+        rope2(__half2float(kr[d]), __half2float(kr[d + D / 2]), float(pos) * a.inv_freq[d], r0, r1);
+        Kc[slot * D + d] = __float2half_rn(r0);
+        Kc[slot * D + d + D / 2] = __float2half_rn(r1);
+      }
+      for (int d = tid; d < D; d += kAW * 32) Vc[slot * D + d] = vr[d];
+      __threadfence();
+    }
+  } else {
+    for (int i = tid; i < rep * CH; i += kAW * 32) {
+      const int r = i / CH, c = i % CH;
+      *reinterpret_cast<uint4*>(q_sm + swz<D>(r, c)) =
+          *reinterpret_cast<const uint4*>(Q + (h * rep + r) * D + c * 8);
+    }
+  }
+  __syncthreads();
+
+  unsigned char* ring = ring_all + warp * (kAStages * 2 * TILE);
+  auto issue = [&](int stage, int b) {
+    if (b < b1) {
+      const long base = (long(bt[b]) * Hkv + h) * BT * D;  // halves
+      const unsigned char* ks = reinterpret_cast<const unsigned char*>(Kc + base);
+      const unsigned char* vs = reinterpret_cast<const unsigned char*>(Vc + base);
+      unsigned char* kd = ring + stage * 2 * TILE;
+      unsigned char* vd = kd + TILE;
+#pragma unroll
+      for (int i = lane; i < BT * CH; i += 32) {
+        const int r = i / CH, c = i % CH;
+        cp_async16a(kd + swz<D>(r, c), ks + i * 16);
+        cp_async16a(vd + swz<D>(r, c), vs + i * 16);
+      }
+    }
+    cp_commit();
+  };
+  issue(0, b0 + warp);
+  issue(1, b0 + warp + kAW);
+
+  // q fragments (rows 8-15 are zero: a1 = a3 = 0)
+  uint32_t qa[KSTEPS][2];
+#pragma unroll
+  for (int kk = 0; kk < KSTEPS; ++kk) {
+    const int r = lane & 7, c = 2 * kk + ((lane >> 3) & 1);
+    ldsm_x2(qa[kk], q_sm + swz<D>(r, c));
+  }
+
+  const float sl2 = a.scale * kLog2e;
+  float o[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+  float m_r = -INFINITY, l_r = 0.f;
+
+  int stage = 0;
+  for (int b = b0 + warp; b < b1; b += kAW) {
+    cp_wait<1>();
+    __syncwarp();
+    const unsigned char* kt = ring + stage * 2 * TILE;
+    const unsigned char* vt = kt + TILE;
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int kk = 0; kk < KSTEPS; ++kk) {
+      uint32_t r[4];
+      const int rr = (lane & 7) + ((lane >> 4) << 3), cc = 2 * kk + ((lane >> 3) & 1);
+      ldsm_x4(r, kt + swz<D>(rr, cc));
+      mma_f16(s[0], qa[kk][0], 0u, qa[kk][1], 0u, r[0], r[1]);
+      mma_f16(s[1], qa[kk][0], 0u, qa[kk][1], 0u, r[2], r[3]);
+    }
+    // scale to log2 units, mask keys past the position, online softmax of row g
+    const int tb = b * BT;
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int tok = tb + 8 * j + 2 * t + e;
+        v[2 * j + e] = tok <= pos ? s[j][e] * sl2 : -INFINITY;
+      }
+    float mx = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m_r, mx);
+    const float corr = exp2f(m_r - m_new);
+    float p[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) p[e] = exp2f(v[e] - m_new);
+    l_r = l_r * corr + (p[0] + p[1] + p[2] + p[3]);
+    m_r = m_new;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      o[nt][0] *= corr;
+      o[nt][1] *= corr;
+    }
+    const uint32_t pa0 = pack_half2(p[0], p[1]), pa2 = pack_half2(p[2], p[3]);
+#pragma unroll
+    for (int np = 0; np < NT / 2; ++np) {
+      uint32_t r[4];
+      const int rr = (lane & 7) + (((lane >> 3) & 1) << 3), cc = 2 * np + (lane >> 4);
+      ldsm_x4_t(r, vt + swz<D>(rr, cc));
+      mma_f16(o[2 * np], pa0, 0u, pa2, 0u, r[0], r[1]);
+      mma_f16(o[2 * np + 1], pa0, 0u, pa2, 0u, r[2], r[3]);
+    }
+    __syncwarp();
+    issue(stage, b + 2 * kAW);
+    stage ^= 1;
+  }
+  cp_wait<0>();
+  l_r += __shfl_xor_sync(0xffffffffu, l_r, 1);
+  l_r += __shfl_xor_sync(0xffffffffu, l_r, 2);
+
+  // ---- merge the warps (rows g < rep hold results)
+  __syncthreads();  // every warp is done with its ring: reuse it
+  float* s_o = reinterpret_cast<float*>(ring_all);  // [kAW][kMaxRepA][D]
+  if (g < rep) {
+    if (t == 0) {
+      s_m[warp][g] = m_r;
+      s_l[warp][g] = l_r;
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      *reinterpret_cast<float2*>(s_o + (warp * kMaxRepA + g) * D + nt * 8 + 2 * t) = make_float2(o[nt][0], o[nt][1]);
+    }
+  }
+  __syncthreads();
+  grid_launch_dependents();
+
+  half* Out = reinterpret_cast<half*>(a.out) + long(row) * Hq * D;
+  const long pbase = (long(row) * Hq + h * rep) * S;
+  for (int e = tid; e < rep * D; e += kAW * 32) {
+    const int hi = e / D, d = e % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAW; ++w)
+      if (s_l[w][hi] > 0.f) M = fmaxf(M, s_m[w][hi]);
+    float num = 0.f, den = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAW; ++w) {
+      if (s_l[w][hi] > 0.f) {
+        const float f = exp2f(s_m[w][hi] - M);
+        num = fmaf(s_o[(w * kMaxRepA + hi) * D + d], f, num);
+        den = fmaf(s_l[w][hi], f, den);
+      }
+    }
+    if (S == 1) {
+      Out[(h * rep + hi) * D + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
+    } else {
+      const long pb = (pbase + long(hi) * S + split);
+      a.part_o[pb * D + d] = num;
+      if (d == 0) *reinterpret_cast<float2*>(a.part_ml + pb * 2) = make_float2(M, den);
+    }
+  }
+  if (S == 1) return;
+
+  // ---- split-KV: the last CTA of (row, h) combines
+  __threadfence();
+  __syncthreads();
+  unsigned* ctr = a.counters + long(row) * Hkv + h;
+  if (tid == 0) s_last = (atomicAdd(ctr, 1u) == unsigned(S - 1)) ? 1 : 0;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int i = tid; i < rep * S; i += kAW * 32) {
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml + (pbase + i) * 2));
+    s_cm[i] = ml.x;
+    s_cl[i] = ml.y;
+  }
+  __syncthreads();
+  if (tid < rep) {
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < S; ++s2)
+      if (s_cl[tid * S + s2] > 0.f) M = fmaxf(M, s_cm[tid * S + s2]);
+    float den = 0.f;
+    for (int s2 = 0; s2 < S; ++s2)
+      if (s_cl[tid * S + s2] > 0.f) den = fmaf(s_cl[tid * S + s2], exp2f(s_cm[tid * S + s2] - M), den);
+    const float inv = den > 0.f ? 1.f / den : 0.f;
+    for (int s2 = 0; s2 < S; ++s2)
+      s_w[tid][s2] = s_cl[tid * S + s2] > 0.f ? exp2f(s_cm[tid * S + s2] - M) * inv : 0.f;
+  }
+  __syncthreads();
+  for (int e = tid; e < rep * D; e += kAW * 32) {
+    const int hi = e / D, d = e % D;
+    const float* po = a.part_o + (pbase + long(hi) * S) * D + d;
+    float num = 0.f;
+#pragma unroll 8
+    for (int s2 = 0; s2 < S; ++s2) num = fmaf(__ldcg(po + long(s2) * D), s_w[hi][s2], num);
+    Out[(h * rep + hi) * D + d] = __float2half_rn(num);
+  }
+  if (tid == 0) *ctr = 0u;
+}
+
+template <int D, bool FUSED>
+nmx_status_t launch_mma(Ctx* c, const AttnArgs& a) {
+  constexpr int TILE = 16 * D * 2;
+  const size_t smem = TILE + size_t(kAW) * kAStages * 2 * TILE;
+  auto kern = paged_decode_mma_kernel<D, FUSED>;
+  static std::mutex mu;
+  static std::map<int, bool> attr;  // per device
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!attr[c->device]) {
+      NMX_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+      attr[c->device] = true;
+    }
+  }
+  return launch(c, kern, dim3(a.splits, a.Hkv, a.T), dim3(kAW * 32), smem, a);
+}
+
+}  // namespace
+
+nmx_status_t paged_attention_mma(Ctx* c, const AttnArgs& a, bool fused) {
+  NMX_CHECK(a.splits >= 1 && a.splits <= kMaxSplitsA, NMX_ERR_UNSUPPORTED, "paged attention: 1..32 splits");
+  if (a.D == 128) return fused ? launch_mma<128, true>(c, a) : launch_mma<128, false>(c, a);
+  if (a.D == 64) return fused ? launch_mma<64, true>(c, a) : launch_mma<64, false>(c, a);
+  NMX_CHECK(false, NMX_ERR_UNSUPPORTED, "paged attention: head_dim must be 64 or 128");
+}
+
+}  // namespace nmx

@@ -105,6 +105,8 @@ struct AttnArgs {
 // fused = 1: apply RoPE to q and append the row's own k/v (one query row per
 // sequence, decode); fused = 0: q is already roped and K/V already appended.
 nmx_status_t paged_attention(Ctx* c, const AttnArgs& a, bool fused);
+// the tensor-core implementation behind paged_attention (attention_mma.cu)
+nmx_status_t paged_attention_mma(Ctx* c, const AttnArgs& a, bool fused);
 
 // RoPE q and k of T new tokens in place in qkv [T, ldq] and write k/v to the
 // pages at each token's position.

@@ -82,15 +82,22 @@ __device__ __forceinline__ void load_words(WordVec<WPT>& out, const uint32_t* p)
 }
 
 // f16x2 A-operand pairs of one packed word (see pair_k for the order).
+// (a & b) | c in one LOP3 (truth table 0xEA)
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+
 template <int BITS>
 __device__ __forceinline__ void dequant_word(uint32_t w, uint32_t* P) {
   if constexpr (BITS == 4) {
-    const uint32_t magic = 0x64006400u;  // f16 1024.0 in both halves
-    P[0] = (w & 0x000F000Fu) | magic;    // 1024 + q0,      1024 + q4
-    P[1] = (w & 0x00F000F0u) | magic;    // 1024 + 16 q1,   1024 + 16 q5
+    const uint32_t magic = 0x64006400u;          // f16 1024.0 in both halves
+    P[0] = and_or(w, 0x000F000Fu, magic);        // 1024 + q0,      1024 + q4
+    P[1] = and_or(w, 0x00F000F0u, magic);        // 1024 + 16 q1,   1024 + 16 q5
     const uint32_t w8 = w >> 8;
-    P[2] = (w8 & 0x000F000Fu) | magic;   // q2, q6
-    P[3] = (w8 & 0x00F000F0u) | magic;   // 16 q3, 16 q7
+    P[2] = and_or(w8, 0x000F000Fu, magic);       // q2, q6
+    P[3] = and_or(w8, 0x00F000F0u, magic);       // 16 q3, 16 q7
   } else {
     P[0] = __byte_perm(w, 0x64646464u, 0x5140);  // 1024 + b0, 1024 + b1
     P[1] = __byte_perm(w, 0x64646464u, 0x7362);  // 1024 + b2, 1024 + b3

@@ -52,7 +52,9 @@ __device__ __forceinline__ unsigned ordered_bits(float v) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-template <int NT, int EPI, int TPT, int STAGES>
+// ONE: a single activation row (M == 1); only the accumulators of column 0
+// (d0, d2 of lanes with t == 0) carry results, so the others are not folded.
+template <int NT, int EPI, int TPT, int STAGES, bool ONE>
 __global__ void __launch_bounds__(kThreads, 2) qgemv_dl_kernel(GemvDLArgs a) {
   constexpr int NCOL = NT * 8;
   constexpr int ROWS = 16 * TPT;
@@ -78,25 +80,24 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_dl_kernel(GemvDLArgs a) {
   const int wg = blockIdx.x * kWarps + warp;
   const int u0 = int((long long)wg * U / W), u1 = int((long long)(wg + 1) * U / W);
 
-  const unsigned char* __restrict__ Wb = reinterpret_cast<const unsigned char*>(a.w);
-  // the issue cursor walks (tile group, block) incrementally: no divisions
-  int is_u = u0, is_tg = u0 / nb, is_blk = u0 - (u0 / nb) * nb;
+  // unit u is record u of the matrix (tile-major, blocks inside a tile), so
+  // the issue cursor is a pointer that advances one record per unit; the
+  // paired up tile sits pair_tiles * nb records further
+  const unsigned char* src_cur = reinterpret_cast<const unsigned char*>(a.w) + size_t(u0) * kRec + 16 * lane;
+  const size_t pair_off = size_t(a.pair_tiles) * nb * kRec;
+  int is_u = u0;
   auto issue = [&](int slot) {
     if (is_u < u1) {
-      unsigned char* dst = ring + size_t(slot) * TPT * kRec;
+      unsigned char* dst = ring + size_t(slot) * TPT * kRec + 16 * lane;
 #pragma unroll
       for (int tp = 0; tp < TPT; ++tp) {
-        const long tile = (tp == 0) ? is_tg : is_tg + a.pair_tiles;
-        const unsigned char* src = Wb + (size_t(tile) * nb + is_blk) * kRec;
-        cp_async16(dst + tp * kRec + 16 * lane, src + 16 * lane);
-        cp_async16(dst + tp * kRec + kRecW + 16 * lane, src + kRecW + 16 * lane);
-        if (lane < 8) cp_async16(dst + tp * kRec + 1024 + 16 * lane, src + 1024 + 16 * lane);
+        const unsigned char* src = src_cur + tp * pair_off;
+        cp_async16(dst + tp * kRec, src);
+        cp_async16(dst + tp * kRec + kRecW, src + kRecW);
+        if (lane < 8) cp_async16(dst + tp * kRec + 1024, src + 1024);
       }
       ++is_u;
-      if (++is_blk == nb) {
-        is_blk = 0;
-        ++is_tg;
-      }
+      src_cur += kRec;
     }
     cp_async_commit();
   };
@@ -319,9 +320,11 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_dl_kernel(GemvDLArgs a) {
           mma16816(d, P0[4], P1[4], P0[5], P1[5], xc.x, xc.y, d[0], d[1], d[2], d[3]);
           mma16816(d, P0[6], P1[6], P0[7], P1[7], xc.z, xc.w, d[0], d[1], d[2], d[3]);
           acc[tp][nt][0] = fmaf(fs0, d[0], fmaf(fb0, cx.y, acc[tp][nt][0]));
-          acc[tp][nt][1] = fmaf(fs0, d[1], fmaf(fb0, cx.w, acc[tp][nt][1]));
           acc[tp][nt][2] = fmaf(fs1, d[2], fmaf(fb1, cx.y, acc[tp][nt][2]));
-          acc[tp][nt][3] = fmaf(fs1, d[3], fmaf(fb1, cx.w, acc[tp][nt][3]));
+          if constexpr (!ONE) {
+            acc[tp][nt][1] = fmaf(fs0, d[1], fmaf(fb0, cx.w, acc[tp][nt][1]));
+            acc[tp][nt][3] = fmaf(fs1, d[3], fmaf(fb1, cx.w, acc[tp][nt][3]));
+          }
         }
       }
     }
@@ -369,7 +372,7 @@ int dl_contrib(int n_tg, int K, int grid) {
   return best;
 }
 
-template <int NT, int EPI, int TPT, int STAGES>
+template <int NT, int EPI, int TPT, int STAGES, bool ONE>
 nmx_status_t launch_dl(Ctx* c, const GemvDLArgs& a0, int M) {
   constexpr int NCOL = NT * 8;
   constexpr int ROWS = 16 * TPT;
@@ -378,19 +381,31 @@ nmx_status_t launch_dl(Ctx* c, const GemvDLArgs& a0, int M) {
   const size_t ring = size_t(kWarps) * (STAGES * TPT * kRec + ROWS * NCOL * 4);
   const size_t smem = align_up(size_t(M) * colstride * 4, 16) + size_t(ng) * NCOL * sizeof(float2) + ring;
   NMX_CHECK(smem <= size_t(kMaxDynSmemDL), NMX_ERR_UNSUPPORTED, "qgemv_dl: staging too large");
-  auto kern = qgemv_dl_kernel<NT, EPI, TPT, STAGES>;
+  auto kern = qgemv_dl_kernel<NT, EPI, TPT, STAGES, ONE>;
   static std::mutex mu;
   static std::map<int, bool> attr_set;
+  static std::map<std::pair<int, size_t>, int> occ;  // (device, smem) → resident CTAs per SM
+  int per_sm = 0;
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!attr_set[c->device]) {
       NMX_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmemDL));
       attr_set[c->device] = true;
     }
+    const auto key = std::make_pair(c->device, smem);
+    auto it = occ.find(key);
+    if (it == occ.end()) {
+      NMX_CUDA_OK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem));
+      occ[key] = per_sm;
+    } else {
+      per_sm = it->second;
+    }
   }
+  NMX_CHECK(per_sm > 0, NMX_ERR_UNSUPPORTED, "qgemv_dl: does not fit on an SM");
   GemvDLArgs a = a0;
   a.M = M;
-  const int grid = dl_grid(c->num_sms, a.ctas_per_sm, a.n_tg, a.K);
+  // the split is static per warp: every CTA must be resident at once
+  const int grid = dl_grid(c->num_sms, std::min(a.ctas_per_sm, per_sm), a.n_tg, a.K);
   a.max_contrib = dl_contrib(a.n_tg, a.K, grid);
   NMX_CHECK(size_t(a.n_tg) * a.max_contrib * ROWS * NCOL <= a.partials_cap, NMX_ERR_UNSUPPORTED,
             "qgemv_dl: partial-sum scratch too small");
@@ -400,13 +415,13 @@ nmx_status_t launch_dl(Ctx* c, const GemvDLArgs& a0, int M) {
 constexpr int kStages1 = 6;  // ring depth, one tile per unit
 constexpr int kStages2 = 3;  // ring depth, gate+up tile pairs
 
-template <int NT>
+template <int NT, bool ONE>
 nmx_status_t dispatch_dl(Ctx* c, const GemvDLArgs& a, int M, int epi) {
   switch (epi) {
-    case EPI_STORE: return launch_dl<NT, EPI_STORE, 1, kStages1>(c, a, M);
-    case EPI_RESID: return launch_dl<NT, EPI_RESID, 1, kStages1>(c, a, M);
-    case EPI_SILU: return launch_dl<NT, EPI_SILU, 2, kStages2>(c, a, M);
-    case EPI_ARGMAX: return launch_dl<NT, EPI_ARGMAX, 1, kStages1>(c, a, M);
+    case EPI_STORE: return launch_dl<NT, EPI_STORE, 1, kStages1, ONE>(c, a, M);
+    case EPI_RESID: return launch_dl<NT, EPI_RESID, 1, kStages1, ONE>(c, a, M);
+    case EPI_SILU: return launch_dl<NT, EPI_SILU, 2, kStages2, ONE>(c, a, M);
+    case EPI_ARGMAX: return launch_dl<NT, EPI_ARGMAX, 1, kStages1, ONE>(c, a, M);
   }
   NMX_CHECK(false, NMX_ERR_UNSUPPORTED, "qgemv_dl: unknown epilogue");
 }
@@ -515,7 +530,14 @@ nmx_status_t qgemv_dl(Ctx* c, const GemvDLArgs& a, int epi) {
     if (a.out_ids) b.out_ids = a.out_ids + m0;
     if (a.next_tokens) b.next_tokens = a.next_tokens + m0;
     b.n_tg = a.N / 16;
-    NMX_TRY(mc <= 8 ? dispatch_dl<1>(c, b, mc, epi) : dispatch_dl<4>(c, b, mc, epi));
+    nmx_status_t st;
+    if (mc == 1)
+      st = dispatch_dl<1, true>(c, b, mc, epi);
+    else if (mc <= 8)
+      st = dispatch_dl<1, false>(c, b, mc, epi);
+    else
+      st = dispatch_dl<4, false>(c, b, mc, epi);
+    NMX_TRY(st);
   }
   return NMX_OK;
 }
