@@ -197,21 +197,26 @@ def run_reference(args, rank: int, world: int) -> None:
 # ------------------------------------------------------------------ GPU leg
 
 def time_gemv_roofline(torch, nmx, ctx, peaks, N=2 * 14336, K=4096, copies=3, reps=30):
-    """Average duration of the decode GEMV at the gate/up shape (M=1,
-    N=28672, K=4096, Q4 g64), rotating over `copies` distinct weight copies
-    so no launch finds its weights in L2."""
+    """Average duration of the decode-record GEMV (the kernel every linear of
+    the decode step runs) at the gate/up shape (M=1, N=28672, K=4096, Q4 g64),
+    rotating over `copies` distinct weight copies so no launch finds its
+    weights in L2. Timed with CUDA events on the library's stream."""
     wf = torch.randn((N, K), device="cuda", dtype=torch.float32) * 0.02
-    ws = [ctx.quantize(wf, 64, 4) for _ in range(copies)]
+    recs = []
+    for _ in range(copies):
+        wq, s, b = ctx.quantize(wf, 64, 4)
+        recs.append(ctx.pack_records(wq, s, b))
+        del wq, s, b
     del wf
     x = torch.randn((1, K), device="cuda", dtype=torch.float16)
     y = torch.empty((1, N), device="cuda", dtype=torch.float16)
     for i in range(5):
-        ctx.quantized_matmul(x, *ws[i % copies], out=y)
+        ctx.quantized_matmul_records(x, recs[i % copies], N, out=y)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(reps):
-        ctx.quantized_matmul(x, *ws[i % copies], out=y)
+        ctx.quantized_matmul_records(x, recs[i % copies], N, out=y)
     e1.record()
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1000.0 / reps
@@ -219,9 +224,24 @@ def time_gemv_roofline(torch, nmx, ctx, peaks, N=2 * 14336, K=4096, copies=3, re
     ach = nbytes / (us * 1e-6) / 1e9
     return {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None,
-            "kernel": f"qgemv_kernel (decode GEMV, M=1, N={N}, K={K}, 4-bit g64)",
+            "kernel": f"qgemv_dl_kernel (decode-record GEMV, M=1, N={N}, K={K}, 4-bit g64)",
             "bytes_per_launch": nbytes, "us_per_launch": round(us, 2),
             "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)"}
+
+
+TRAFFIC_PROFILE = ROOT / "profiles" / "qgemv_dl_m1_n28672_k4096.md"
+
+
+def profiled_traffic():
+    """DRAM bytes (read + write) per launch of the roofline kernel, from the
+    committed ncu summary of the same shape (`traffic_bytes_per_launch:`)."""
+    try:
+        for line in TRAFFIC_PROFILE.read_text().splitlines():
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
 
 
 def time_c1(torch, ctx, peaks, copies=32, reps=64):
@@ -286,8 +306,10 @@ def _run_ours(args, rank, world, dist, torch, nmx, ctx, peaks, dev):
         barrier()
         torch.cuda.synchronize()
         e0.record()
+        torch.cuda.nvtx.range_push("timed")  # lets a profiler capture only the timed steps
         for _ in range(args.steps):
             step()
+        torch.cuda.nvtx.range_pop()
         e1.record()
         torch.cuda.synchronize()
         barrier()
@@ -323,12 +345,7 @@ def _run_ours(args, rank, world, dist, torch, nmx, ctx, peaks, dev):
 
     roof = time_gemv_roofline(torch, nmx, ctx, peaks)
     c1 = time_c1(torch, ctx, peaks)
-    traffic_file = ROOT / "profiles" / "traffic.json"
-    if traffic_file.exists():
-        try:
-            roof["traffic"] = json.loads(traffic_file.read_text()).get("qgemv_gateup_bytes_per_launch")
-        except Exception:
-            pass
+    roof["traffic"] = profiled_traffic()
     step_bytes = model.step_weight_bytes + model.kv_bytes_per_token * (PROMPT + GEN // 2)
     per_gpu_tps = value / world
     step_gbs = step_bytes * per_gpu_tps / 1e9

@@ -34,6 +34,18 @@ nmx_status_t ctx_workspace(Ctx* c, size_t bytes, void** out) {
   return NMX_OK;
 }
 
+nmx_status_t ctx_check_device_error(Ctx* c) {
+  unsigned v = 0;
+  NMX_CUDA_OK(cudaMemcpy(&v, c->dev_err, sizeof(v), cudaMemcpyDeviceToHost));
+  if (v != 0) {
+    NMX_CUDA_OK(cudaMemset(c->dev_err, 0, sizeof(v)));
+    set_error("a kernel gave up a bounded wait (device error word " + std::to_string(v) + "); results of the "
+              "work since the last check are not valid");
+    return NMX_ERR_CUDA;
+  }
+  return NMX_OK;
+}
+
 nmx_status_t ctx_counters(Ctx* c, size_t n, unsigned** out) {
   if (n > c->n_counters) {
     if (c->counters) {
@@ -88,6 +100,16 @@ NMX_API nmx_status_t nmx_ctx_create(int device, nmx_ctx_t* out) {
     return NMX_ERR_CUDA;
   }
   h->c.owns_stream = true;
+  e = cudaMalloc(reinterpret_cast<void**>(&h->c.dev_err), 256);
+  if (e == cudaSuccess) e = cudaMemset(h->c.dev_err, 0, 256);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    if (h->c.dev_err) cudaFree(h->c.dev_err);
+    cudaStreamDestroy(h->c.stream);
+    delete h;
+    set_error(std::string("error word: ") + cudaGetErrorString(e));
+    return NMX_ERR_CUDA;
+  }
   *out = h;
   return NMX_OK;
 }
@@ -98,6 +120,7 @@ static void ctx_release(nmx_ctx_t ctx) {
   if (ctx->c.stream) cudaStreamSynchronize(ctx->c.stream);
   if (ctx->c.ws) cudaFree(ctx->c.ws);
   if (ctx->c.counters) cudaFree(ctx->c.counters);
+  if (ctx->c.dev_err) cudaFree(ctx->c.dev_err);
   if (ctx->c.owns_stream && ctx->c.stream) cudaStreamDestroy(ctx->c.stream);
   delete ctx;
 }
@@ -136,7 +159,7 @@ NMX_API nmx_status_t nmx_ctx_synchronize(nmx_ctx_t ctx) {
   API_BEGIN;
   REQUIRE(ctx, "context");
   NMX_CUDA_OK(cudaStreamSynchronize(ctx->c.stream));
-  return NMX_OK;
+  return ctx_check_device_error(&ctx->c);
 }
 
 NMX_API uint64_t nmx_ctx_kernel_launches(nmx_ctx_t ctx) { return ctx ? ctx->c.launches : 0; }
@@ -190,7 +213,7 @@ NMX_API nmx_status_t nmx_op_qmatmul_records(nmx_ctx_t ctx, const void* x, const 
   REQUIRE(x, "x");
   REQUIRE(records, "records");
   REQUIRE(y, "y");
-  NMX_CHECK(qgemv_dl_supported(4, 64, NMX_F16, N, K), NMX_ERR_UNSUPPORTED, "nmx_op_qmatmul_records: N % 16, K % 128");
+  NMX_CHECK(qgemv_dl_supported(4, 64, NMX_F16, N, K), NMX_ERR_UNSUPPORTED, "nmx_op_qmatmul_records: needs N % 16 == 0, K % 128 == 0, (N/16)*(K/128) >= 8");
   NMX_CHECK(reinterpret_cast<uintptr_t>(records) % 16 == 0, NMX_ERR_INVALID, "records must be 16-byte aligned");
   Ctx* c = &ctx->c;
   GemvDLArgs a;
@@ -200,7 +223,7 @@ NMX_API nmx_status_t nmx_op_qmatmul_records(nmx_ctx_t ctx, const void* x, const 
   unsigned* ctr = nullptr;
   NMX_TRY(ctx_counters(c, size_t(N / 16), &ctr));
   a.x = x; a.ldx = K; a.w = records; a.N = N; a.K = K; a.M = M; a.y = y; a.ldy = N;
-  a.partials = static_cast<float*>(ws); a.partials_cap = pf; a.counters = ctr;
+  a.partials = static_cast<float*>(ws); a.partials_cap = pf; a.counters = ctr; a.err = c->dev_err;
   return qgemv_dl(c, a, EPI_STORE);
 }
 

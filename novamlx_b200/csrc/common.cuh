@@ -61,9 +61,15 @@ struct Ctx {
   size_t ws_bytes = 0;
   unsigned* counters = nullptr;  // zeroed, reset by kernels after use
   size_t n_counters = 0;
+  // device word that kernels set when a bounded wait runs out (bit 0);
+  // read and cleared by nmx_ctx_synchronize
+  unsigned* dev_err = nullptr;
 };
 
 nmx_status_t ctx_workspace(Ctx* c, size_t bytes, void** out);
+// after the stream has drained: NMX_ERR_CUDA if a kernel reported a wait
+// that ran out (the word is cleared)
+nmx_status_t ctx_check_device_error(Ctx* c);
 nmx_status_t ctx_counters(Ctx* c, size_t n, unsigned** out);
 
 // ---------------------------------------------------------- dtype traits

@@ -70,12 +70,21 @@ struct GemvDLArgs {
   int max_contrib = 0;                // slot stride (set per launch)
   unsigned* counters = nullptr;       // [n_tg], zero between launches
   int ctas_per_sm = 2;
+  // the records are never written on this stream while the launch may be in
+  // flight (model weights): the weight stream may start before the
+  // programmatic-launch wait
+  bool weights_static = false;
+  unsigned* err = nullptr;            // device word: bit 0 = a bounded wait ran out
 };
 bool qgemv_dl_supported(int bits, int gs, nmx_dtype_t dt, int N, int K);
 int qgemv_dl_max_m(int K, int epi);
 // floats of partial-sum scratch one launch of this shape may need
 size_t qgemv_dl_partials_floats(int N_out, int K, int epi, int num_sms, int ctas_per_sm);
 nmx_status_t qgemv_dl(Ctx* c, const GemvDLArgs& a, int epi);
+// 1..8 activation rows (qgemv_dl dispatches here when the staging fits)
+bool qgemv_small_fits(int M, int N_out, int K, int epi, int num_sms);
+size_t qgemv_small_partials_floats(int N_out, int K, int epi, int num_sms);
+nmx_status_t qgemv_small(Ctx* c, const GemvDLArgs& a, int epi);
 // MLX-layout parts (mask 1 = words, 2 = scales, 4 = biases) of rows
 // [row0, row0 + rows) to decode records, and back.
 nmx_status_t repack_to_records(Ctx* c, const uint32_t* wq, const void* s, const void* b, int rows, int K,

@@ -512,6 +512,8 @@ nmx_status_t Model::linear(const Lin& l, const void* x, long ldx, const void* ga
     a.logits_f32 = logits_f32; a.keys = dl_keys; a.done = dl_done; a.out_ids = ids; a.next_tokens = next_tokens;
     a.partials = dl_partials; a.partials_cap = dl_partials_cap; a.counters = dl_counters;
     a.ctas_per_sm = dl_ctas_per_sm;
+    a.weights_static = true;
+    a.err = ctx->dev_err;
     return qgemv_dl(ctx, a, epi);
   }
   GemvArgs a;
@@ -728,7 +730,16 @@ nmx_status_t Model::forward(KvPool* pool, const nmx_seq_t* seqs, int n, nmx_out_
   } else {
     NMX_CUDA_OK(cudaMemcpyAsync(out_host, out_ids, size_t(out_rows) * 4, cudaMemcpyDeviceToHost, c->stream));
   }
-  NMX_CUDA_OK(cudaStreamSynchronize(c->stream));
+  return finish_step();
+}
+
+// read the device error word with the step's results, then wait for both
+nmx_status_t Model::finish_step() {
+  unsigned* perr = reinterpret_cast<unsigned*>(pinned + pinned_bytes - 4);
+  *perr = 0u;
+  NMX_CUDA_OK(cudaMemcpyAsync(perr, ctx->dev_err, 4, cudaMemcpyDeviceToHost, ctx->stream));
+  NMX_CUDA_OK(cudaStreamSynchronize(ctx->stream));
+  if (*perr != 0u) return ctx_check_device_error(ctx);
   return NMX_OK;
 }
 
@@ -773,8 +784,7 @@ nmx_status_t Model::decode_greedy(KvPool* pool, const int32_t* first, const int3
   for (int s = 0; s < steps; ++s) NMX_TRY(run_decode_graph(pool, n));
   if (out_host && steps > 0)
     NMX_CUDA_OK(cudaMemcpyAsync(out_host, hist, size_t(steps) * n * 4, cudaMemcpyDeviceToHost, c->stream));
-  NMX_CUDA_OK(cudaStreamSynchronize(c->stream));
-  return NMX_OK;
+  return finish_step();
 }
 
 }  // namespace nmx

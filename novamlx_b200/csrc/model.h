@@ -102,6 +102,7 @@ struct Model {
   nmx_status_t run_decode_graph(KvPool* pool, int B);
   nmx_status_t upload_batch(const nmx_seq_t* seqs, int n, int* T_out, bool* decode_out);
   nmx_status_t forward(KvPool* pool, const nmx_seq_t* seqs, int n, nmx_out_mode_t mode, void* out_host);
+  nmx_status_t finish_step();
   nmx_status_t decode_greedy(KvPool* pool, const int32_t* first, const int32_t* start, const int32_t* tables,
                              int max_blocks, int n, int steps, int32_t* out_host);
 };

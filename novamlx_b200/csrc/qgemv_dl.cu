@@ -5,8 +5,10 @@
 //   [   0,  512)  lane l = 4g+t: 16 B = words (2t, 2t+1) of groups 2B and
 //                 2B+1 of row 16T+g (the words lane l feeds to the MMA)
 //   [ 512, 1024)  the same for row 16T+g+8
-//   [1024, 1088)  scales  s[row 0..15][group 0..1]  (f16)
-//   [1088, 1152)  biases  b[row 0..15][group 0..1]  (f16)
+//   [1024, 1152)  scales, then biases (f16): entry (kind, group gi, g) at
+//                 1024 + ((kind * 2 + gi) * 8 + g) * 4 holds the pair
+//                 (row 16T+g, row 16T+g+8), so one 4-byte load gives a lane
+//                 the coefficient of both rows its MMA accumulators cover
 // Records of a tile are consecutive in k, tiles consecutive in rows, so a
 // linear is one stream of 1152-byte records and holds exactly the bytes of
 // its MLX form (packed words + scales + biases).
@@ -52,9 +54,7 @@ __device__ __forceinline__ unsigned ordered_bits(float v) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// ONE: a single activation row (M == 1); only the accumulators of column 0
-// (d0, d2 of lanes with t == 0) carry results, so the others are not folded.
-template <int NT, int EPI, int TPT, int STAGES, bool ONE>
+template <int NT, int EPI, int TPT, int STAGES>
 __global__ void __launch_bounds__(kThreads, 2) qgemv_dl_kernel(GemvDLArgs a) {
   constexpr int NCOL = NT * 8;
   constexpr int ROWS = 16 * TPT;
@@ -102,7 +102,9 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_dl_kernel(GemvDLArgs a) {
     cp_async_commit();
   };
 
-  // weights never change during a step: start streaming before the wait
+  // model weights never change during a step: start streaming them before
+  // the wait (records an op-level caller may just have written are not)
+  if (!a.weights_static) grid_wait();
 #pragma unroll
   for (int s = 0; s < STAGES; ++s) issue(s);
 
@@ -290,10 +292,11 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_dl_kernel(GemvDLArgs a) {
       const unsigned char* rec = rec0 + tp * kRec;
       const uint4 w0 = *reinterpret_cast<const uint4*>(rec + 16 * lane);
       const uint4 w1 = *reinterpret_cast<const uint4*>(rec + kRecW + 16 * lane);
-      const __half2 s0 = *reinterpret_cast<const __half2*>(rec + 1024 + 4 * g);
-      const __half2 s1 = *reinterpret_cast<const __half2*>(rec + 1024 + 4 * (g + 8));
-      const __half2 b0 = *reinterpret_cast<const __half2*>(rec + 1088 + 4 * g);
-      const __half2 b1 = *reinterpret_cast<const __half2*>(rec + 1088 + 4 * (g + 8));
+      // (row g, row g+8) pairs of scales / biases of groups 0 and 1
+      const __half2 sA = *reinterpret_cast<const __half2*>(rec + 1024 + 4 * g);
+      const __half2 sB = *reinterpret_cast<const __half2*>(rec + 1056 + 4 * g);
+      const __half2 bA = *reinterpret_cast<const __half2*>(rec + 1088 + 4 * g);
+      const __half2 bB = *reinterpret_cast<const __half2*>(rec + 1120 + 4 * g);
 #pragma unroll
       for (int gi = 0; gi < 2; ++gi) {
         const int G = 2 * blk + gi;
@@ -302,10 +305,8 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_dl_kernel(GemvDLArgs a) {
         dequant_word<4>(gi ? w0.w : w0.y, P0 + 4);
         dequant_word<4>(gi ? w1.z : w1.x, P1);
         dequant_word<4>(gi ? w1.w : w1.y, P1 + 4);
-        const float fs0 = gi ? __high2float(s0) : __low2float(s0);
-        const float fs1 = gi ? __high2float(s1) : __low2float(s1);
-        const float fb0 = gi ? __high2float(b0) : __low2float(b0);
-        const float fb1 = gi ? __high2float(b1) : __low2float(b1);
+        const float fs0 = __low2float(gi ? sB : sA), fs1 = __high2float(gi ? sB : sA);
+        const float fb0 = __low2float(gi ? bB : bA), fb1 = __high2float(gi ? bB : bA);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           int col = nt * 8 + g;
@@ -321,10 +322,8 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_dl_kernel(GemvDLArgs a) {
           mma16816(d, P0[6], P1[6], P0[7], P1[7], xc.z, xc.w, d[0], d[1], d[2], d[3]);
           acc[tp][nt][0] = fmaf(fs0, d[0], fmaf(fb0, cx.y, acc[tp][nt][0]));
           acc[tp][nt][2] = fmaf(fs1, d[2], fmaf(fb1, cx.y, acc[tp][nt][2]));
-          if constexpr (!ONE) {
-            acc[tp][nt][1] = fmaf(fs0, d[1], fmaf(fb0, cx.w, acc[tp][nt][1]));
-            acc[tp][nt][3] = fmaf(fs1, d[3], fmaf(fb1, cx.w, acc[tp][nt][3]));
-          }
+          acc[tp][nt][1] = fmaf(fs0, d[1], fmaf(fb0, cx.w, acc[tp][nt][1]));
+          acc[tp][nt][3] = fmaf(fs1, d[3], fmaf(fb1, cx.w, acc[tp][nt][3]));
         }
       }
     }
@@ -372,7 +371,7 @@ int dl_contrib(int n_tg, int K, int grid) {
   return best;
 }
 
-template <int NT, int EPI, int TPT, int STAGES, bool ONE>
+template <int NT, int EPI, int TPT, int STAGES>
 nmx_status_t launch_dl(Ctx* c, const GemvDLArgs& a0, int M) {
   constexpr int NCOL = NT * 8;
   constexpr int ROWS = 16 * TPT;
@@ -381,7 +380,7 @@ nmx_status_t launch_dl(Ctx* c, const GemvDLArgs& a0, int M) {
   const size_t ring = size_t(kWarps) * (STAGES * TPT * kRec + ROWS * NCOL * 4);
   const size_t smem = align_up(size_t(M) * colstride * 4, 16) + size_t(ng) * NCOL * sizeof(float2) + ring;
   NMX_CHECK(smem <= size_t(kMaxDynSmemDL), NMX_ERR_UNSUPPORTED, "qgemv_dl: staging too large");
-  auto kern = qgemv_dl_kernel<NT, EPI, TPT, STAGES, ONE>;
+  auto kern = qgemv_dl_kernel<NT, EPI, TPT, STAGES>;
   static std::mutex mu;
   static std::map<int, bool> attr_set;
   static std::map<std::pair<int, size_t>, int> occ;  // (device, smem) → resident CTAs per SM
@@ -415,13 +414,13 @@ nmx_status_t launch_dl(Ctx* c, const GemvDLArgs& a0, int M) {
 constexpr int kStages1 = 6;  // ring depth, one tile per unit
 constexpr int kStages2 = 3;  // ring depth, gate+up tile pairs
 
-template <int NT, bool ONE>
+template <int NT>
 nmx_status_t dispatch_dl(Ctx* c, const GemvDLArgs& a, int M, int epi) {
   switch (epi) {
-    case EPI_STORE: return launch_dl<NT, EPI_STORE, 1, kStages1, ONE>(c, a, M);
-    case EPI_RESID: return launch_dl<NT, EPI_RESID, 1, kStages1, ONE>(c, a, M);
-    case EPI_SILU: return launch_dl<NT, EPI_SILU, 2, kStages2, ONE>(c, a, M);
-    case EPI_ARGMAX: return launch_dl<NT, EPI_ARGMAX, 1, kStages1, ONE>(c, a, M);
+    case EPI_STORE: return launch_dl<NT, EPI_STORE, 1, kStages1>(c, a, M);
+    case EPI_RESID: return launch_dl<NT, EPI_RESID, 1, kStages1>(c, a, M);
+    case EPI_SILU: return launch_dl<NT, EPI_SILU, 2, kStages2>(c, a, M);
+    case EPI_ARGMAX: return launch_dl<NT, EPI_ARGMAX, 1, kStages1>(c, a, M);
   }
   NMX_CHECK(false, NMX_ERR_UNSUPPORTED, "qgemv_dl: unknown epilogue");
 }
@@ -461,27 +460,18 @@ __global__ void repack_kernel(const uint32_t* wq, const half* s, const half* b, 
     }
     if (t == 0) {
       for (int hf = 0; hf < 2; ++hf) {
-        const int rr = g + 8 * hf;
-        const long row = tl * 16 + rr;
-        half* rs = reinterpret_cast<half*>(r + 1024) + rr * 2;
-        half* rb = reinterpret_cast<half*>(r + 1088) + rr * 2;
+        const long row = tl * 16 + g + 8 * hf;
         const long sb = row * ng + 2 * blk;
-        if (part_mask & 2) {
-          if (!inverse) {
-            rs[0] = s[sb];
-            rs[1] = s[sb + 1];
-          } else {
-            s_out[sb] = rs[0];
-            s_out[sb + 1] = rs[1];
+        for (int gi = 0; gi < 2; ++gi) {
+          half* rs = reinterpret_cast<half*>(r + 1024 + ((0 * 2 + gi) * 8 + g) * 4) + hf;
+          half* rb = reinterpret_cast<half*>(r + 1024 + ((1 * 2 + gi) * 8 + g) * 4) + hf;
+          if (part_mask & 2) {
+            if (!inverse) *rs = s[sb + gi];
+            else s_out[sb + gi] = *rs;
           }
-        }
-        if (part_mask & 4) {
-          if (!inverse) {
-            rb[0] = b[sb];
-            rb[1] = b[sb + 1];
-          } else {
-            b_out[sb] = rb[0];
-            b_out[sb + 1] = rb[1];
+          if (part_mask & 4) {
+            if (!inverse) *rb = b[sb + gi];
+            else b_out[sb + gi] = *rb;
           }
         }
       }
@@ -496,11 +486,14 @@ size_t qgemv_dl_partials_floats(int N_out, int K, int epi, int num_sms, int ctas
   const int n_tg = N_out / 16;
   const int rows = epi == EPI_SILU ? 32 : 16;
   const int grid = dl_grid(num_sms, ctas_per_sm, n_tg, K);
-  return size_t(n_tg) * dl_contrib(n_tg, K, grid) * rows * 32;
+  return std::max(size_t(n_tg) * dl_contrib(n_tg, K, grid) * rows * 32,
+                  qgemv_small_partials_floats(N_out, K, epi, num_sms));
 }
 
+// at least one (tile group, block) unit per warp of a CTA
 bool qgemv_dl_supported(int bits, int gs, nmx_dtype_t dt, int N, int K) {
-  return bits == 4 && gs == 64 && dt == NMX_F16 && N % 16 == 0 && K % 128 == 0;
+  return bits == 4 && gs == 64 && dt == NMX_F16 && N % 16 == 0 && K % 128 == 0 &&
+         (long long)(N / 16) * (K / 128) >= kWarps;
 }
 
 int qgemv_dl_max_m(int K, int epi) {
@@ -516,7 +509,29 @@ int qgemv_dl_max_m(int K, int epi) {
 }
 
 nmx_status_t qgemv_dl(Ctx* c, const GemvDLArgs& a, int epi) {
-  NMX_CHECK(a.M > 0 && a.N % 16 == 0 && a.K % 128 == 0, NMX_ERR_UNSUPPORTED, "qgemv_dl: bad shape");
+  NMX_CHECK(a.M > 0 && a.N % 16 == 0 && a.K % 128 == 0 && (long long)(a.N / 16) * (a.K / 128) >= kWarps,
+            NMX_ERR_UNSUPPORTED, "qgemv_dl: bad shape");
+  // up to eight rows: the small-batch kernel, in as few launches as its
+  // staging allows
+  if (a.M <= 8) {
+    int mc = a.M;
+    while (mc > 0 && !qgemv_small_fits(mc, a.N, a.K, epi, c->num_sms)) --mc;
+    if (mc > 0) {
+      for (int m0 = 0; m0 < a.M; m0 += mc) {
+        GemvDLArgs b = a;
+        b.M = std::min(mc, a.M - m0);
+        b.x = static_cast<const char*>(a.x) + size_t(m0) * a.ldx * 2;
+        if (a.y) b.y = static_cast<char*>(a.y) + size_t(m0) * a.ldy * 2;
+        if (a.res) b.res = static_cast<const char*>(a.res) + size_t(m0) * a.ldres * 2;
+        if (a.logits_f32) b.logits_f32 = a.logits_f32 + size_t(m0) * a.N;
+        if (a.out_ids) b.out_ids = a.out_ids + m0;
+        if (a.next_tokens) b.next_tokens = a.next_tokens + m0;
+        b.n_tg = a.N / 16;
+        NMX_TRY(qgemv_small(c, b, epi));
+      }
+      return NMX_OK;
+    }
+  }
   const int mmax = qgemv_dl_max_m(a.K, epi);
   NMX_CHECK(mmax > 0, NMX_ERR_UNSUPPORTED, "qgemv_dl: K too large");
   NMX_CHECK(epi != EPI_ARGMAX || a.M <= mmax, NMX_ERR_UNSUPPORTED, "qgemv_dl: argmax needs one launch");
@@ -531,12 +546,10 @@ nmx_status_t qgemv_dl(Ctx* c, const GemvDLArgs& a, int epi) {
     if (a.next_tokens) b.next_tokens = a.next_tokens + m0;
     b.n_tg = a.N / 16;
     nmx_status_t st;
-    if (mc == 1)
-      st = dispatch_dl<1, true>(c, b, mc, epi);
-    else if (mc <= 8)
-      st = dispatch_dl<1, false>(c, b, mc, epi);
+    if (mc <= 8)
+      st = dispatch_dl<1>(c, b, mc, epi);
     else
-      st = dispatch_dl<4, false>(c, b, mc, epi);
+      st = dispatch_dl<4>(c, b, mc, epi);
     NMX_TRY(st);
   }
   return NMX_OK;

@@ -110,7 +110,7 @@ def test_qmatmul_shapes(env, M, N, K, bits, gs):
 
 
 @pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 8, 9, 13, 32])
-@pytest.mark.parametrize("N,K", [(4096, 4096), (256, 512), (4096, 14336), (768, 512)])
+@pytest.mark.parametrize("N,K", [(4096, 4096), (256, 512), (4096, 14336), (768, 512), (6144, 4096), (5120, 1024)])
 def test_qmatmul_records(env, M, N, K):
     """The decode-record GEMV (the model's layout) equals the oracle."""
     torch, nmx, ctx = env
@@ -124,6 +124,31 @@ def test_qmatmul_records(env, M, N, K):
     got = O.f16bits_to_f32(host16(y))
     for m in range(M):
         assert O.max_rel_err(got[m], ref[m]) <= 2e-3, (m, M)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 6144, 4096), (1, 4096, 4096), (3, 5120, 1024), (1, 512, 640 // 128 * 128)])
+def test_qmatmul_records_deterministic(env, M, N, K):
+    """Split tile groups are summed in a fixed order: repeated calls agree bit for bit."""
+    torch, nmx, ctx = env
+    rng = np.random.default_rng(N + K + M)
+    w = rng.standard_normal((N, K), dtype=np.float32) * 0.02
+    wq, s, b = O.quantize(w, 4, 64)
+    x = u16(torch, O.f32_to_f16bits(rng.standard_normal((M, K), dtype=np.float32)))
+    rec = ctx.pack_records(dev(torch, wq.view(np.int32)), u16(torch, s), u16(torch, b))
+    ys = [host16(ctx.quantized_matmul_records(x, rec, N)) for _ in range(4)]
+    for y in ys[1:]:
+        assert np.array_equal(y, ys[0])
+
+
+def test_qmatmul_records_rejects_tiny(env):
+    """Fewer than eight (tile group, block) units: not served by the records kernel."""
+    torch, nmx, ctx = env
+    wq, s, b = O.quantize(np.ones((16, 128), np.float32), 4, 64)
+    rec = ctx.pack_records(dev(torch, wq.view(np.int32)), u16(torch, s), u16(torch, b))
+    x = u16(torch, O.f32_to_f16bits(np.ones((1, 128), np.float32)))
+    with pytest.raises(nmx.NmxError) as e:
+        ctx.quantized_matmul_records(x, rec, 16)
+    assert e.value.status == nmx.NMX_ERR_UNSUPPORTED
 
 
 def test_qmatmul_bf16(env):
