@@ -8,13 +8,18 @@
 // per block runs S = Q·Kᵀ (mma.sync m16n8k16, f16 in, f32 out), an online
 // softmax in the log2 domain on the accumulator fragments, and O += P·V with
 // P taken straight from the S fragments and V fed by ldmatrix.trans. The
-// warps' states merge through shared memory; splits are merged by the last
-// CTA of (row, kv head) to finish (atomic ticket, no waiting), with the
-// per-split weights computed once and the partial rows read in parallel.
+// warps' states merge through shared memory. The splits of one (row, kv
+// head) run as one thread-block cluster (<= 16 CTAs): after a cluster
+// barrier each CTA reads the others' (max, denominator) and numerators
+// through distributed shared memory and writes its slice of the outputs; no
+// global scratch, atomics or fences.
 //
-// In decode (FUSED) the CTA also applies RoPE to q and, when its split holds
-// the new position, writes the new token's roped k and its v to the page
-// before any warp reads it.
+// In decode (FUSED) the CTA also applies RoPE to q; the split holding the new
+// position writes the new token's roped k and its v to the page (for later
+// steps) and adds the token to the softmax from shared memory, so the pages
+// this kernel reads are never written by it or by the kernel before it: with
+// kv_static the K/V stream starts before the programmatic-launch wait.
+#include <algorithm>
 #include <map>
 #include <mutex>
 
@@ -28,7 +33,7 @@ namespace {
 constexpr int kAW = 4;        // warps per CTA
 constexpr int kAStages = 2;   // cp.async stages per warp
 constexpr int kMaxRepA = 8;   // q heads per kv head
-constexpr int kMaxSplitsA = 32;
+constexpr int kMaxClusterA = 16;  // key splits per (row, kv head): one cluster
 
 __device__ __forceinline__ void cp_async16a(void* smem_dst, const void* gsrc) {
   const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
@@ -84,6 +89,27 @@ __device__ __forceinline__ void rope2(float a, float b, float ang, float& ra, fl
   rb = b * cs + a * sn;
 }
 
+__device__ __forceinline__ unsigned cluster_rank() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// all threads of all CTAs of the cluster; orders shared-memory writes before
+// the barrier against reads of them (also remote ones) after it
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// a float in the shared memory of CTA `rank` of the cluster, at the address
+// `p` has in this CTA
+__device__ __forceinline__ float ld_dsmem(const void* p, unsigned rank) {
+  const unsigned la = static_cast<unsigned>(__cvta_generic_to_shared(p));
+  unsigned ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+  return v;
+}
+
 template <int D, bool FUSED>
 __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) {
   constexpr int BT = 16;
@@ -95,66 +121,32 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
   extern __shared__ __align__(128) unsigned char sm[];
   unsigned char* q_sm = sm;
   unsigned char* ring_all = sm + TILE;
-  __shared__ float s_m[kAW][kMaxRepA], s_l[kAW][kMaxRepA];
-  __shared__ float s_w[kMaxRepA][kMaxSplitsA];
-  __shared__ float s_cm[kMaxRepA * kMaxSplitsA], s_cl[kMaxRepA * kMaxSplitsA];
-  __shared__ int s_last;
+  // per-warp softmax states; entry kAW is the new token (FUSED, owner split)
+  __shared__ float s_m[kAW + 1][kMaxRepA], s_l[kAW + 1][kMaxRepA];
+  __shared__ float c_ml[kMaxRepA][2];  // this split's (max, denominator) per q head
+  __shared__ float s_cm[kMaxRepA][kMaxClusterA], s_cl[kMaxRepA][kMaxClusterA];
+  __shared__ float s_w[kMaxRepA][kMaxClusterA];
+  __shared__ __align__(16) half s_knew[D];
+  __shared__ __align__(16) half s_vnew[D];
 
   const int split = blockIdx.x, h = blockIdx.y, row = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   const int Hq = a.Hq, Hkv = a.Hkv, rep = Hq / Hkv, S = gridDim.x;
-
-  grid_wait();
-  const int seq = a.tok_seq[row];
-  const int pos = a.tok_pos[row];
-  const int nblk = (pos + 1 + BT - 1) / BT;
-  const int bps = (nblk + S - 1) / S;
-  const int b0 = split * bps;
-  const int b1 = min(nblk, b0 + bps);
-  const int* bt = a.block_tables + long(seq) * a.max_blocks;
   half* Kc = reinterpret_cast<half*>(a.k_cache);
   half* Vc = reinterpret_cast<half*>(a.v_cache);
-  const half* Q = reinterpret_cast<const half*>(a.q) + long(row) * a.ldq;
 
-  // ---- q tile: rows < rep hold the (roped) q heads, rows >= rep are zero
-  for (int i = tid; i < (BT - rep) * CH; i += kAW * 32) {
-    const int r = rep + i / CH, c = i % CH;
-    *reinterpret_cast<uint4*>(q_sm + swz<D>(r, c)) = make_uint4(0, 0, 0, 0);
-  }
-  if (FUSED) {
-    for (int i = tid; i < rep * (D / 2); i += kAW * 32) {
-      const int hi = i / (D / 2), d = i % (D / 2);
-      const int hq = h * rep + hi;
-      float r0, r1;
-      rope2(__half2float(Q[hq * D + d]), __half2float(Q[hq * D + d + D / 2]), float(pos) * a.inv_freq[d], r0, r1);
-      half* q0 = reinterpret_cast<half*>(q_sm + swz<D>(hi, d / 8)) + (d % 8);
-      half* q1 = reinterpret_cast<half*>(q_sm + swz<D>(hi, (d + D / 2) / 8)) + (d % 8);
-      *q0 = __float2half_rn(r0);
-      *q1 = __float2half_rn(r1);
-    }
-    if (pos >= b0 * BT && pos < b1 * BT) {
-      const long slot = (long(bt[pos / BT]) * Hkv + h) * BT + pos % BT;
-      const half* kr = Q + (Hq + h) * D;
-      const half* vr = Q + (Hq + Hkv + h) * D;
-      for (int d = tid; d < D / 2; d += kAW * 32) {
-        float r0, r1;
-        rope2(__half2float(kr[d]), __half2float(kr[d + D / 2]), float(pos) * a.inv_freq[d], r0, r1);
-        Kc[slot * D + d] = __float2half_rn(r0);
-        Kc[slot * D + d + D / 2] = __float2half_rn(r1);
-      }
-      for (int d = tid; d < D; d += kAW * 32) Vc[slot * D + d] = vr[d];
-      __threadfence();
-    }
-  } else {
-    for (int i = tid; i < rep * CH; i += kAW * 32) {
-      const int r = i / CH, c = i % CH;
-      *reinterpret_cast<uint4*>(q_sm + swz<D>(r, c)) =
-          *reinterpret_cast<const uint4*>(Q + (h * rep + r) * D + c * 8);
-    }
-  }
-  __syncthreads();
-
+  int pos = 0, b0 = 0, b1 = 0;
+  const int* bt = nullptr;
+  auto locate = [&]() {
+    const int seq = a.tok_seq[row];
+    pos = a.tok_pos[row];
+    const int nblk = (pos + 1 + BT - 1) / BT;
+    const int bps = (nblk + S - 1) / S;
+    b0 = split * bps;
+    b1 = min(nblk, b0 + bps);
+    bt = a.block_tables + long(seq) * a.max_blocks;
+  };
   unsigned char* ring = ring_all + warp * (kAStages * 2 * TILE);
   auto issue = [&](int stage, int b) {
     if (b < b1) {
@@ -172,8 +164,68 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
     }
     cp_commit();
   };
-  issue(0, b0 + warp);
-  issue(1, b0 + warp + kAW);
+  // The pages read here never hold the new token (FUSED masks it and adds it
+  // from registers), so when the caller says the cache is not written by the
+  // previous kernel, the stream starts before the programmatic-launch wait.
+  if (a.kv_static) {
+    locate();
+    issue(0, b0 + warp);
+    issue(1, b0 + warp + kAW);
+    grid_wait();
+  } else {
+    grid_wait();
+    locate();
+    issue(0, b0 + warp);
+    issue(1, b0 + warp + kAW);
+  }
+  const half* Q = reinterpret_cast<const half*>(a.q) + long(row) * a.ldq;
+  const int bpos = pos / BT;
+  const bool owner = FUSED && bpos >= b0 && bpos < b1;
+
+  // ---- q tile: rows < rep hold the (roped) q heads, rows >= rep are zero
+  for (int i = tid; i < (BT - rep) * CH; i += kAW * 32) {
+    const int r = rep + i / CH, c = i % CH;
+    *reinterpret_cast<uint4*>(q_sm + swz<D>(r, c)) = make_uint4(0, 0, 0, 0);
+  }
+  if (FUSED) {
+    for (int i = tid; i < rep * (D / 2); i += kAW * 32) {
+      const int hi = i / (D / 2), d = i % (D / 2);
+      const int hq = h * rep + hi;
+      float r0, r1;
+      rope2(__half2float(Q[hq * D + d]), __half2float(Q[hq * D + d + D / 2]), float(pos) * a.inv_freq[d], r0, r1);
+      half* q0 = reinterpret_cast<half*>(q_sm + swz<D>(hi, d / 8)) + (d % 8);
+      half* q1 = reinterpret_cast<half*>(q_sm + swz<D>(hi, (d + D / 2) / 8)) + (d % 8);
+      *q0 = __float2half_rn(r0);
+      *q1 = __float2half_rn(r1);
+    }
+    if (owner) {
+      // the new token: roped k and v to its page (for later steps) and to
+      // shared memory (for this one)
+      const long slot = (long(bt[bpos]) * Hkv + h) * BT + pos % BT;
+      const half* kr = Q + (Hq + h) * D;
+      const half* vr = Q + (Hq + Hkv + h) * D;
+      for (int d = tid; d < D / 2; d += kAW * 32) {
+        float r0, r1;
+        rope2(__half2float(kr[d]), __half2float(kr[d + D / 2]), float(pos) * a.inv_freq[d], r0, r1);
+        const half k0 = __float2half_rn(r0), k1 = __float2half_rn(r1);
+        Kc[slot * D + d] = k0;
+        Kc[slot * D + d + D / 2] = k1;
+        s_knew[d] = k0;
+        s_knew[d + D / 2] = k1;
+      }
+      for (int d = tid; d < D; d += kAW * 32) {
+        Vc[slot * D + d] = vr[d];
+        s_vnew[d] = vr[d];
+      }
+    }
+  } else {
+    for (int i = tid; i < rep * CH; i += kAW * 32) {
+      const int r = i / CH, c = i % CH;
+      *reinterpret_cast<uint4*>(q_sm + swz<D>(r, c)) =
+          *reinterpret_cast<const uint4*>(Q + (h * rep + r) * D + c * 8);
+    }
+  }
+  __syncthreads();
 
   // q fragments (rows 8-15 are zero: a1 = a3 = 0)
   uint32_t qa[KSTEPS][2];
@@ -184,6 +236,8 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
   }
 
   const float sl2 = a.scale * kLog2e;
+  // keys up to `last` come from the pages (FUSED: the new token is added apart)
+  const int last = FUSED ? pos - 1 : pos;
   float o[NT][4];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
@@ -204,7 +258,7 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
       mma_f16(s[0], qa[kk][0], 0u, qa[kk][1], 0u, r[0], r[1]);
       mma_f16(s[1], qa[kk][0], 0u, qa[kk][1], 0u, r[2], r[3]);
     }
-    // scale to log2 units, mask keys past the position, online softmax of row g
+    // scale to log2 units, mask keys past `last`, online softmax of row g
     const int tb = b * BT;
     float v[4];
 #pragma unroll
@@ -212,16 +266,18 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int tok = tb + 8 * j + 2 * t + e;
-        v[2 * j + e] = tok <= pos ? s[j][e] * sl2 : -INFINITY;
+        v[2 * j + e] = tok <= last ? s[j][e] * sl2 : -INFINITY;
       }
     float mx = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
     const float m_new = fmaxf(m_r, mx);
-    const float corr = exp2f(m_r - m_new);
+    // a block with every key masked leaves the state as it was
+    const float m_use = m_new == -INFINITY ? 0.f : m_new;
+    const float corr = exp2f(m_r - m_use);
     float p[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) p[e] = exp2f(v[e] - m_new);
+    for (int e = 0; e < 4; ++e) p[e] = exp2f(v[e] - m_use);
     l_r = l_r * corr + (p[0] + p[1] + p[2] + p[3]);
     m_r = m_new;
 #pragma unroll
@@ -246,9 +302,10 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
   l_r += __shfl_xor_sync(0xffffffffu, l_r, 1);
   l_r += __shfl_xor_sync(0xffffffffu, l_r, 2);
 
-  // ---- merge the warps (rows g < rep hold results)
+  // ---- merge the warps (rows g < rep hold results) and the new token
   __syncthreads();  // every warp is done with its ring: reuse it
-  float* s_o = reinterpret_cast<float*>(ring_all);  // [kAW][kMaxRepA][D]
+  float* s_o = reinterpret_cast<float*>(ring_all);           // [kAW][kMaxRepA][D]
+  float* c_num = s_o + kAW * kMaxRepA * D;                   // [kMaxRepA][D] this split's numerators
   if (g < rep) {
     if (t == 0) {
       s_m[warp][g] = m_r;
@@ -259,16 +316,33 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
       *reinterpret_cast<float2*>(s_o + (warp * kMaxRepA + g) * D + nt * 8 + 2 * t) = make_float2(o[nt][0], o[nt][1]);
     }
   }
+  if (warp == 0) {
+    // new token score per q head: f16 q · f16 k summed in f32, log2 units
+    for (int hi = 0; hi < rep; ++hi) {
+      float sc = 0.f;
+      if (owner) {
+        for (int d = lane; d < D; d += 32) {
+          const half qv = reinterpret_cast<const half*>(q_sm + swz<D>(hi, d / 8))[d % 8];
+          sc = fmaf(__half2float(qv), __half2float(s_knew[d]), sc);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, off);
+      }
+      if (lane == 0) {
+        s_m[kAW][hi] = owner ? sc * sl2 : -INFINITY;
+        s_l[kAW][hi] = owner ? 1.f : 0.f;
+      }
+    }
+  }
   __syncthreads();
   grid_launch_dependents();
 
   half* Out = reinterpret_cast<half*>(a.out) + long(row) * Hq * D;
-  const long pbase = (long(row) * Hq + h * rep) * S;
   for (int e = tid; e < rep * D; e += kAW * 32) {
     const int hi = e / D, d = e % D;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kAW; ++w)
+    for (int w = 0; w <= kAW; ++w)
       if (s_l[w][hi] > 0.f) M = fmaxf(M, s_m[w][hi]);
     float num = 0.f, den = 0.f;
 #pragma unroll
@@ -279,55 +353,57 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
         den = fmaf(s_l[w][hi], f, den);
       }
     }
+    if (s_l[kAW][hi] > 0.f) {
+      const float f = exp2f(s_m[kAW][hi] - M);
+      num = fmaf(__half2float(s_vnew[d]), f, num);
+      den += f;
+    }
     if (S == 1) {
       Out[(h * rep + hi) * D + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
     } else {
-      const long pb = (pbase + long(hi) * S + split);
-      a.part_o[pb * D + d] = num;
-      if (d == 0) *reinterpret_cast<float2*>(a.part_ml + pb * 2) = make_float2(M, den);
+      c_num[hi * D + d] = num;
+      if (d == 0) {
+        c_ml[hi][0] = M;
+        c_ml[hi][1] = den;
+      }
     }
   }
   if (S == 1) return;
 
-  // ---- split-KV: the last CTA of (row, h) combines
-  __threadfence();
-  __syncthreads();
-  unsigned* ctr = a.counters + long(row) * Hkv + h;
-  if (tid == 0) s_last = (atomicAdd(ctr, 1u) == unsigned(S - 1)) ? 1 : 0;
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  for (int i = tid; i < rep * S; i += kAW * 32) {
-    const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml + (pbase + i) * 2));
-    s_cm[i] = ml.x;
-    s_cl[i] = ml.y;
+  // ---- split-KV: the splits of (row, h) are one cluster; each CTA combines
+  // a slice of the outputs from the others' shared memory
+  cluster_sync();
+  if (tid < rep * S) {
+    const int hi = tid / S, s2 = tid % S;
+    s_cm[hi][s2] = ld_dsmem(&c_ml[hi][0], unsigned(s2));
+    s_cl[hi][s2] = ld_dsmem(&c_ml[hi][1], unsigned(s2));
   }
   __syncthreads();
   if (tid < rep) {
     float M = -INFINITY;
     for (int s2 = 0; s2 < S; ++s2)
-      if (s_cl[tid * S + s2] > 0.f) M = fmaxf(M, s_cm[tid * S + s2]);
+      if (s_cl[tid][s2] > 0.f) M = fmaxf(M, s_cm[tid][s2]);
     float den = 0.f;
     for (int s2 = 0; s2 < S; ++s2)
-      if (s_cl[tid * S + s2] > 0.f) den = fmaf(s_cl[tid * S + s2], exp2f(s_cm[tid * S + s2] - M), den);
+      if (s_cl[tid][s2] > 0.f) den = fmaf(s_cl[tid][s2], exp2f(s_cm[tid][s2] - M), den);
     const float inv = den > 0.f ? 1.f / den : 0.f;
-    for (int s2 = 0; s2 < S; ++s2)
-      s_w[tid][s2] = s_cl[tid * S + s2] > 0.f ? exp2f(s_cm[tid * S + s2] - M) * inv : 0.f;
+    for (int s2 = 0; s2 < S; ++s2) s_w[tid][s2] = s_cl[tid][s2] > 0.f ? exp2f(s_cm[tid][s2] - M) * inv : 0.f;
   }
   __syncthreads();
-  for (int e = tid; e < rep * D; e += kAW * 32) {
+  const int E = rep * D, e0 = split * E / S, e1 = (split + 1) * E / S;
+  for (int e = e0 + tid; e < e1; e += kAW * 32) {
     const int hi = e / D, d = e % D;
-    const float* po = a.part_o + (pbase + long(hi) * S) * D + d;
     float num = 0.f;
-#pragma unroll 8
-    for (int s2 = 0; s2 < S; ++s2) num = fmaf(__ldcg(po + long(s2) * D), s_w[hi][s2], num);
+    for (int s2 = 0; s2 < S; ++s2)
+      if (s_w[hi][s2] != 0.f) num = fmaf(ld_dsmem(c_num + hi * D + d, unsigned(s2)), s_w[hi][s2], num);
     Out[(h * rep + hi) * D + d] = __float2half_rn(num);
   }
-  if (tid == 0) *ctr = 0u;
+  // no CTA leaves while another may still read its shared memory
+  cluster_sync();
 }
 
 template <int D, bool FUSED>
-nmx_status_t launch_mma(Ctx* c, const AttnArgs& a) {
+nmx_status_t launch_mma(Ctx* c, const AttnArgs& a, int S) {
   constexpr int TILE = 16 * D * 2;
   const size_t smem = TILE + size_t(kAW) * kAStages * 2 * TILE;
   auto kern = paged_decode_mma_kernel<D, FUSED>;
@@ -337,18 +413,50 @@ nmx_status_t launch_mma(Ctx* c, const AttnArgs& a) {
     std::lock_guard<std::mutex> lk(mu);
     if (!attr[c->device]) {
       NMX_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+      NMX_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
       attr[c->device] = true;
     }
   }
-  return launch(c, kern, dim3(a.splits, a.Hkv, a.T), dim3(kAW * 32), smem, a);
+  // the largest cluster not above S that the device can place
+  static std::map<std::pair<int, int>, int> fit;  // (device, S) → usable S
+  int s_use = S;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = fit.find({c->device, S});
+    if (it != fit.end()) {
+      s_use = it->second;
+    } else {
+      while (s_use > 1) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(s_use, a.Hkv, 1);
+        cfg.blockDim = dim3(kAW * 32);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = s_use;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) break;
+        cudaGetLastError();
+        s_use = s_use > 8 ? 8 : s_use / 2;
+      }
+      fit[{c->device, S}] = s_use;
+    }
+  }
+  return launch_cluster(c, kern, dim3(s_use, a.Hkv, a.T), dim3(kAW * 32), smem, unsigned(s_use), a);
 }
 
 }  // namespace
 
 nmx_status_t paged_attention_mma(Ctx* c, const AttnArgs& a, bool fused) {
-  NMX_CHECK(a.splits >= 1 && a.splits <= kMaxSplitsA, NMX_ERR_UNSUPPORTED, "paged attention: 1..32 splits");
-  if (a.D == 128) return fused ? launch_mma<128, true>(c, a) : launch_mma<128, false>(c, a);
-  if (a.D == 64) return fused ? launch_mma<64, true>(c, a) : launch_mma<64, false>(c, a);
+  NMX_CHECK(a.splits >= 1, NMX_ERR_UNSUPPORTED, "paged attention: splits >= 1");
+  // the splits of one (row, kv head) form a cluster: at most 16 CTAs
+  const int S = std::min(a.splits, kMaxClusterA);
+  if (a.D == 128) return fused ? launch_mma<128, true>(c, a, S) : launch_mma<128, false>(c, a, S);
+  if (a.D == 64) return fused ? launch_mma<64, true>(c, a, S) : launch_mma<64, false>(c, a, S);
   NMX_CHECK(false, NMX_ERR_UNSUPPORTED, "paged attention: head_dim must be 64 or 128");
 }
 

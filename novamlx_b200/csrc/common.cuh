@@ -133,6 +133,33 @@ nmx_status_t launch(Ctx* c, void (*kern)(KArgs...), dim3 grid, dim3 block, size_
   return NMX_OK;
 }
 
+// As launch, with CTAs grouped in clusters of cluster_x along x (1 = none).
+template <typename... KArgs, typename... Args>
+nmx_status_t launch_cluster(Ctx* c, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, unsigned cluster_x,
+                            Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = c->stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cluster_x;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = cluster_x > 1 ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e != cudaSuccess) {
+    set_error(std::string("kernel launch (cluster ") + std::to_string(cluster_x) + "): " + cudaGetErrorString(e));
+    return NMX_ERR_CUDA;
+  }
+  c->launches++;
+  return NMX_OK;
+}
+
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 }  // namespace nmx

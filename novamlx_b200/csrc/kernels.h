@@ -110,6 +110,9 @@ struct AttnArgs {
   int T = 0, Hq = 0, Hkv = 0, D = 0, BT = 16;
   int splits = 1;
   float scale = 1.0f;
+  // the pages are not written by the kernel before this one on the stream
+  // (true in the decode step): the K/V stream may start before its wait
+  bool kv_static = false;
 };
 // fused = 1: apply RoPE to q and append the row's own k/v (one query row per
 // sequence, decode); fused = 0: q is already roped and K/V already appended.

@@ -35,7 +35,7 @@ namespace {
 
 constexpr int kBT = 16;             // tokens per KV block
 constexpr int kBlockCap = 4096;     // block-table columns per sequence (65,536 tokens)
-constexpr int kMaxSplits = 32;      // split-KV CTAs per (sequence, kv head)
+constexpr int kMaxSplits = 16;      // split-KV CTAs per (sequence, kv head): one cluster
 constexpr int kHistCap = 1 << 16;   // decode-loop id history entries
 
 size_t dsize(nmx_dtype_t dt) { return dt == NMX_F32 || dt == NMX_U32 || dt == NMX_I32 ? 4 : 2; }
@@ -545,6 +545,7 @@ nmx_status_t Model::run_layers_decode(KvPool* pool, int B) {
     at.out = attn; at.part_o = part_o; at.part_ml = part_ml; at.counters = attn_counters;
     at.T = B; at.Hq = cf.n_heads; at.Hkv = cf.n_kv_heads; at.D = cf.head_dim; at.BT = kBT;
     at.splits = splits; at.scale = 1.0f / std::sqrt(float(cf.head_dim));
+    at.kv_static = true;
     NMX_TRY(paged_attention(c, at, true));
 
     NMX_TRY(linear(ly.o, attn, Nq, nullptr, B, H, 0, nullptr, h, H, h, H, EPI_RESID));
