@@ -224,7 +224,7 @@ def time_gemv_roofline(torch, nmx, ctx, peaks, N=2 * 14336, K=4096, copies=3, re
     ach = nbytes / (us * 1e-6) / 1e9
     return {"bound": "hbm", "achieved": round(ach, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": round(ach / peaks["hbm_gbs"], 4), "traffic": None,
-            "kernel": f"qgemv_dl_kernel (decode-record GEMV, M=1, N={N}, K={K}, 4-bit g64)",
+            "kernel": f"qgemv_dl8_kernel (decode-record GEMV, M=1, N={N}, K={K}, 4-bit g64)",
             "bytes_per_launch": nbytes, "us_per_launch": round(us, 2),
             "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)"}
 

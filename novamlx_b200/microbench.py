@@ -2,12 +2,18 @@
 
   python -m novamlx_b200.microbench gemv [--n 28672] [--k 4096] [--m 1]
   python -m novamlx_b200.microbench attn [--batch 1] [--ctx 2176]
+  python -m novamlx_b200.microbench decode [--layers 2] [--ctx 2048] [--tokens 64]
 
 gemv: the decode-record GEMV (nmx_op_qmatmul_records) over `copies` distinct
 weight copies, so the weights come from HBM on every launch.
 attn: paged decode attention (nmx_op_attn_paged_decode) at Llama-3.1-8B
 head shapes (32 query heads, 8 KV heads, head dim 128, 16-token pages) over
 a pool larger than L2, each rep reading a different set of pages.
+
+decode: the model's batch-1 decode step (nmx_decode_greedy) on the
+Llama-3.1-8B architecture cut to --layers layers (random 4-bit weights), at
+context --ctx; the per-token time, and one short decode inside an NVTX range
+named "decode" for a profiler to select.
 
 Prints one JSON line per run with the average launch duration measured by
 CUDA events on the library's stream and the algorithmic bytes per launch.
@@ -65,28 +71,59 @@ def attn(ctx, torch, batch, ctx_len, reps, hq=32, hkv=8, d=128, bt=16):
             "bytes": nbytes, "gbs": round(nbytes / us / 1e3, 1)}
 
 
+def decode(ctx, torch, nmx, layers, ctx_len, tokens):
+    import numpy as np
+    cfg = nmx.llama31_8b(n_layers=layers, max_batch=1, max_tokens=ctx_len)
+    m = nmx.Model(ctx, cfg)
+    m.init_random(seed=0, std=0.02)
+    nblk = (ctx_len + tokens + 15) // 16 + 1
+    pool = nmx.KVPool(m, nblk + 4)
+    table = np.arange(nblk, dtype=np.int32)
+    prompt = np.random.default_rng(0).integers(0, cfg.vocab, ctx_len)
+    first = int(m.forward(pool, [dict(tokens=prompt, start_pos=0, block_table=table)])[0])
+    for _ in range(3):
+        m.decode_greedy(pool, [first], [ctx_len], table[None], 8, want_ids=False)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    m.decode_greedy(pool, [first], [ctx_len], table[None], tokens, want_ids=False)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / tokens
+    torch.cuda.nvtx.range_push("decode")
+    m.decode_greedy(pool, [first], [ctx_len], table[None], 2, want_ids=False)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
+    return {"what": "decode step", "layers": layers, "ctx": ctx_len, "us_per_token": round(us, 2),
+            "weight_bytes_per_token": m.step_weight_bytes}
+
+
 def main():
     import torch
 
     from novamlx_b200 import nmx
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemv", "attn"])
+    ap.add_argument("what", choices=["gemv", "attn", "decode"])
     ap.add_argument("--n", type=int, default=28672)
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--copies", type=int, default=3)
     ap.add_argument("--batch", type=int, default=1)
-    ap.add_argument("--ctx", type=int, default=2176)
+    ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--reps", type=int, default=30)
+    ap.add_argument("--layers", type=int, default=2)
+    ap.add_argument("--tokens", type=int, default=64)
     a = ap.parse_args()
     torch.cuda.set_device(0)
     c = nmx.Context(0)
     with torch.cuda.stream(c.stream):
         if a.what == "gemv":
             r = gemv(c, torch, a.n, a.k, a.m, a.copies, a.reps)
-        else:
+        elif a.what == "attn":
             r = attn(c, torch, a.batch, a.ctx, a.reps)
+        else:
+            r = decode(c, torch, nmx, a.layers, a.ctx, a.tokens)
     print(json.dumps(r), flush=True)
 
 
