@@ -258,6 +258,13 @@ NMX_API uint64_t nmx_model_weight_bytes(nmx_model_t model);
 /* Bytes the weights of one decode step read (every linear once, one
  * embedding row, norms). */
 NMX_API uint64_t nmx_model_step_weight_bytes(nmx_model_t model);
+/* Batch-1 decode schedule (no counterpart in the reference, which has no
+ * kernel schedule to choose): enable != 0 runs batch-1 nmx_decode_greedy,
+ * and batch-1 nmx_forward decode steps that return ids, as one persistent
+ * cooperative launch; 0 (the default) uses one CUDA graph of per-layer
+ * kernels per step. Both give the same ids up to floating-point summation
+ * order. */
+NMX_API nmx_status_t nmx_model_set_persistent_decode(nmx_model_t model, int enable);
 
 /* Paged KV pool: num_blocks blocks of block_tokens tokens, fp16 K and V for
  * every layer. Layout per layer: [num_blocks][Hkv][block_tokens][head_dim]

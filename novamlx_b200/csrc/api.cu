@@ -396,6 +396,13 @@ NMX_API nmx_status_t nmx_model_get_tensor(nmx_model_t model, const char* name, v
 NMX_API uint64_t nmx_model_weight_bytes(nmx_model_t model) { return model ? model->m->wbytes : 0; }
 NMX_API uint64_t nmx_model_step_weight_bytes(nmx_model_t model) { return model ? model->m->step_bytes : 0; }
 
+NMX_API nmx_status_t nmx_model_set_persistent_decode(nmx_model_t model, int enable) {
+  API_BEGIN;
+  REQUIRE(model, "model");
+  model->m->persistent_enabled = enable != 0;
+  return NMX_OK;
+}
+
 NMX_API nmx_status_t nmx_kv_pool_create(nmx_model_t model, int block_tokens, int num_blocks, nmx_kv_pool_t* out) {
   API_BEGIN;
   REQUIRE(model, "model");

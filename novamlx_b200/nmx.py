@@ -96,6 +96,7 @@ _proto("nmx_model_load_tensor", _i, _vp, C.c_char_p, _vp, _i, C.POINTER(C.c_int6
 _proto("nmx_model_get_tensor", _i, _vp, C.c_char_p, _vp, _sz)
 _proto("nmx_model_weight_bytes", _u64, _vp)
 _proto("nmx_model_step_weight_bytes", _u64, _vp)
+_proto("nmx_model_set_persistent_decode", _i, _vp, _i)
 _proto("nmx_kv_pool_create", _i, _vp, _i, _i, C.POINTER(_vp))
 _proto("nmx_kv_pool_destroy", _i, _vp)
 _proto("nmx_kv_copy_blocks", _i, _vp, _ip, _ip, _i)
@@ -447,6 +448,10 @@ class Model:
     @property
     def step_weight_bytes(self) -> int:
         return int(lib.nmx_model_step_weight_bytes(self.h))
+
+    def set_persistent_decode(self, enable: bool) -> None:
+        """Batch-1 decode as one persistent launch, or (default) a graph of per-layer kernels."""
+        check(lib.nmx_model_set_persistent_decode(self.h, 1 if enable else 0))
 
     @property
     def kv_bytes_per_token(self) -> int:

@@ -223,3 +223,40 @@ def test_wide_layer_matches_oracle(ctx):
         ids = m.forward(pool, [dict(tokens=[tok], start_pos=pos, block_table=table)], nmx.OUT_ARGMAX_LAST)
         assert ids[0] == int(np.argmax(g[0]))
         pos += 1
+
+
+@pytest.mark.parametrize("name", ["llama", "qwen"])
+def test_persistent_decode_matches_graph_decode(ctx, name):
+    """Batch-1 greedy decode as one persistent launch equals the per-layer
+    kernel graph (same pages, same ids), and its first step's id is the
+    argmax of the oracle's logits teacher-forced on the same tokens."""
+    from novamlx_b200 import nmx
+    m, om, cfg = build(ctx, name)
+    pool = nmx.KVPool(m, 40)
+    rng = np.random.default_rng(21)
+    P, S = 37, 24
+    prompt = rng.integers(0, cfg.vocab, P)
+    table = rng.permutation(40)[:8].astype(np.int32)
+    runs = []
+    for persistent in (True, False):
+        m.set_persistent_decode(persistent)
+        first = m.forward(pool, [dict(tokens=prompt, start_pos=0, block_table=table)], nmx.OUT_ARGMAX_LAST)
+        n0 = ctx.launches
+        runs.append((first.copy(), m.decode_greedy(pool, first, [P], table[None], S)))
+        if persistent:
+            assert ctx.launches - n0 == 1  # every step in one launch
+    m.set_persistent_decode(True)
+    assert np.array_equal(runs[0][0], runs[1][0])
+    assert np.array_equal(runs[0][1], runs[1][1])
+    # the host-facing batch-1 decode step (persistent, steps = 1) agrees too
+    m.forward(pool, [dict(tokens=prompt, start_pos=0, block_table=table)], nmx.OUT_ARGMAX_LAST)
+    cur = int(runs[0][0][0])
+    for s in range(4):
+        cur = int(m.forward(pool, [dict(tokens=[cur], start_pos=P + s, block_table=table)], nmx.OUT_ARGMAX_LAST)[0])
+        assert cur == runs[0][1][s, 0]
+    c = om.new_cache(64)
+    om.forward(c, prompt, 0)
+    r = om.forward(c, [int(runs[0][0][0])], P)
+    top2 = np.sort(r[0])[-2:]
+    if top2[1] - top2[0] > 1e-2:  # no near-tie: the id is determined
+        assert int(np.argmax(r[0])) == runs[0][1][0, 0]
