@@ -81,6 +81,12 @@ int qgemv_dl_max_m(int K, int epi);
 // floats of partial-sum scratch one launch of this shape may need
 size_t qgemv_dl_partials_floats(int N_out, int K, int epi, int num_sms, int ctas_per_sm);
 nmx_status_t qgemv_dl(Ctx* c, const GemvDLArgs& a, int epi);
+// tensor-core (tcgen05) GEMM over decode records for many rows (prefill):
+// store / residual / SiLU·up epilogues, no RMSNorm prologue (normalise x
+// first); N_out % 256 (SiLU: % 128) and K % 128
+bool qgemm_tc_supported(int N_out, int K, int epi);
+nmx_status_t qgemm_tc(Ctx* c, const GemvDLArgs& a, int epi);
+constexpr int kGemmMinRows = 64;  // qgemv_dl hands row counts from here on to qgemm_tc
 // 1..8 activation rows (qgemv_dl dispatches here when the staging fits)
 bool qgemv_small_fits(int M, int N_out, int K, int epi, int num_sms);
 size_t qgemv_small_partials_floats(int N_out, int K, int epi, int num_sms);

@@ -176,6 +176,7 @@ nmx_status_t Model::create(Ctx* c, const nmx_model_cfg& cfg, Model** out) {
       {&m->q_roped, size_t(T) * Nq * es},
       {&m->attn, size_t(T) * Nq * es},
       {&m->act, size_t(T) * F * es},
+      {&m->xn, size_t(T) * H * es},
       {&m->last_h, size_t(rows_logits) * H * es},
       {reinterpret_cast<void**>(&m->logits_f32), size_t(rows_logits) * V * 4},
       {reinterpret_cast<void**>(&m->part_o), size_t(B) * cfg.n_heads * kMaxSplits * cfg.head_dim * 4},
@@ -506,6 +507,20 @@ KvPool::~KvPool() {
 nmx_status_t Model::linear(const Lin& l, const void* x, long ldx, const void* gamma, int M, int N_out,
                            long pair_off_rows, const void* bias, void* y, long ldy, const void* res, long ldres,
                            int epi, float* logits_f32, int* ids, int* next_tokens) {
+  if (l.dl && M >= kGemmMinRows && qgemm_tc_supported(N_out, l.K, epi)) {
+    // many rows (prefill): the tensor-core GEMM, after the RMSNorm it has no
+    // prologue for
+    if (gamma) {
+      NMX_TRY(rmsnorm(ctx, x, ldx, gamma, M, l.K, cfg.rms_eps, NMX_F16, xn, l.K));
+      x = xn;
+      ldx = l.K;
+    }
+    GemvDLArgs a;
+    a.x = x; a.ldx = ldx; a.w = l.w; a.N = N_out; a.K = l.K; a.M = M; a.pair_tiles = pair_off_rows / 16;
+    a.bias = bias; a.y = y; a.ldy = ldy; a.res = res; a.ldres = ldres;
+    a.err = ctx->dev_err;
+    return qgemm_tc(ctx, a, epi);
+  }
   if (l.dl) {
     GemvDLArgs a;
     a.x = x; a.ldx = ldx; a.gamma = gamma; a.eps = cfg.rms_eps; a.w = l.w;

@@ -55,6 +55,7 @@ struct Model {
   // workspace
   char* wsbase = nullptr;
   void *h = nullptr, *qkv = nullptr, *q_roped = nullptr, *attn = nullptr, *act = nullptr, *last_h = nullptr;
+  void* xn = nullptr;  // RMSNorm output for the tensor-core GEMM (prefill)
   float* logits_f32 = nullptr;
   float *part_o = nullptr, *part_ml = nullptr;
   unsigned* attn_counters = nullptr;

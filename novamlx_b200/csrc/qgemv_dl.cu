@@ -511,6 +511,9 @@ int qgemv_dl_max_m(int K, int epi) {
 nmx_status_t qgemv_dl(Ctx* c, const GemvDLArgs& a, int epi) {
   NMX_CHECK(a.M > 0 && a.N % 16 == 0 && a.K % 128 == 0 && (long long)(a.N / 16) * (a.K / 128) >= kWarps,
             NMX_ERR_UNSUPPORTED, "qgemv_dl: bad shape");
+  // many rows: the tensor-core GEMM
+  if (a.M >= kGemmMinRows && a.gamma == nullptr && a.err != nullptr && qgemm_tc_supported(a.N, a.K, epi))
+    return qgemm_tc(c, a, epi);
   // up to eight rows: the small-batch kernel, in as few launches as its
   // staging allows
   if (a.M <= 8) {

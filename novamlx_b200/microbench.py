@@ -1,11 +1,14 @@
 """Per-kernel timings of the decode path, one kernel at a time.
 
   python -m novamlx_b200.microbench gemv [--n 28672] [--k 4096] [--m 1]
+  python -m novamlx_b200.microbench gemm [--m 2048] [--n 4096] [--k 4096]
   python -m novamlx_b200.microbench attn [--batch 1] [--ctx 2176]
   python -m novamlx_b200.microbench decode [--layers 2] [--ctx 2048] [--tokens 64]
 
 gemv: the decode-record GEMV (nmx_op_qmatmul_records) over `copies` distinct
 weight copies, so the weights come from HBM on every launch.
+gemm: the same entry point with many rows (the tcgen05 prefill GEMM); dense
+f16 TFLOP/s = 2·M·N·K / t.
 attn: paged decode attention (nmx_op_attn_paged_decode) at Llama-3.1-8B
 head shapes (32 query heads, 8 KV heads, head dim 128, 16-token pages) over
 a pool larger than L2, each rep reading a different set of pages.
@@ -22,6 +25,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import time
 
 
 def _time(torch, fn, reps, warm=5):
@@ -53,6 +57,19 @@ def gemv(ctx, torch, n, k, m, copies, reps):
             "gbs": round(nbytes / us / 1e3, 1)}
 
 
+def gemm(ctx, torch, m, n, k, reps):
+    wf = torch.randn((n, k), device="cuda", dtype=torch.float32) * 0.02
+    wq, s, b = ctx.quantize(wf, 64, 4)
+    rec = ctx.pack_records(wq, s, b)
+    del wf, wq, s, b
+    x = torch.randn((m, k), device="cuda", dtype=torch.float16)
+    y = torch.empty((m, n), device="cuda", dtype=torch.float16)
+    us = _time(torch, lambda i: ctx.quantized_matmul_records(x, rec, n, out=y), reps)
+    flops = 2.0 * m * n * k
+    return {"kernel": "qgemm_tc_kernel", "m": m, "n": n, "k": k, "us": round(us, 2),
+            "tflops": round(flops / us / 1e6, 1)}
+
+
 def attn(ctx, torch, batch, ctx_len, reps, hq=32, hkv=8, d=128, bt=16):
     nblk = (ctx_len + bt - 1) // bt
     # enough page sets that the pool (K and V) exceeds L2
@@ -81,6 +98,10 @@ def decode(ctx, torch, nmx, layers, ctx_len, tokens):
     table = np.arange(nblk, dtype=np.int32)
     prompt = np.random.default_rng(0).integers(0, cfg.vocab, ctx_len)
     first = int(m.forward(pool, [dict(tokens=prompt, start_pos=0, block_table=table)])[0])
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    m.forward(pool, [dict(tokens=prompt, start_pos=0, block_table=table)])
+    prefill_ms = (time.perf_counter() - t0) * 1000.0
     for _ in range(3):
         m.decode_greedy(pool, [first], [ctx_len], table[None], 8, want_ids=False)
     torch.cuda.synchronize()
@@ -95,7 +116,7 @@ def decode(ctx, torch, nmx, layers, ctx_len, tokens):
     torch.cuda.synchronize()
     torch.cuda.nvtx.range_pop()
     return {"what": "decode step", "layers": layers, "ctx": ctx_len, "us_per_token": round(us, 2),
-            "weight_bytes_per_token": m.step_weight_bytes}
+            "prefill_ms": round(prefill_ms, 2), "weight_bytes_per_token": m.step_weight_bytes}
 
 
 def main():
@@ -104,10 +125,10 @@ def main():
     from novamlx_b200 import nmx
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemv", "attn", "decode"])
-    ap.add_argument("--n", type=int, default=28672)
+    ap.add_argument("what", choices=["gemv", "gemm", "attn", "decode"])
+    ap.add_argument("--n", type=int, default=None, help="gemv: 28672, gemm: 4096")
     ap.add_argument("--k", type=int, default=4096)
-    ap.add_argument("--m", type=int, default=1)
+    ap.add_argument("--m", type=int, default=None, help="gemv: 1, gemm: 2048")
     ap.add_argument("--copies", type=int, default=3)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--ctx", type=int, default=2048)
@@ -115,11 +136,17 @@ def main():
     ap.add_argument("--layers", type=int, default=2)
     ap.add_argument("--tokens", type=int, default=64)
     a = ap.parse_args()
+    if a.n is None:
+        a.n = 4096 if a.what == "gemm" else 28672
+    if a.m is None:
+        a.m = 2048 if a.what == "gemm" else 1
     torch.cuda.set_device(0)
     c = nmx.Context(0)
     with torch.cuda.stream(c.stream):
         if a.what == "gemv":
             r = gemv(c, torch, a.n, a.k, a.m, a.copies, a.reps)
+        elif a.what == "gemm":
+            r = gemm(c, torch, a.m, a.n, a.k, a.reps)
         elif a.what == "attn":
             r = attn(c, torch, a.batch, a.ctx, a.reps)
         else:

@@ -260,3 +260,25 @@ def test_persistent_decode_matches_graph_decode(ctx, name):
     top2 = np.sort(r[0])[-2:]
     if top2[1] - top2[0] > 1e-2:  # no near-tie: the id is determined
         assert int(np.argmax(r[0])) == runs[0][1][0, 0]
+
+
+@pytest.mark.parametrize("name", ["llama", "qwen"])
+def test_prefill_tensor_core_path_matches_oracle(ctx, name):
+    """A prompt long enough for the tcgen05 GEMM path (>= 64 rows, ragged
+    last tile), then decode steps over the pages it wrote."""
+    from novamlx_b200 import nmx
+    m, om, cfg = build(ctx, name)
+    pool = nmx.KVPool(m, 64)
+    rng = np.random.default_rng(31)
+    prompt = rng.integers(0, cfg.vocab, 130)
+    table = rng.permutation(64)[:12].astype(np.int32)
+    got = m.forward(pool, [dict(tokens=prompt, start_pos=0, block_table=table)], nmx.OUT_LOGITS_ALL)
+    cache = om.new_cache(192)
+    ref = om.forward(cache, prompt, 0, all_logits=True)
+    check_logits(got, ref)
+    pos = len(prompt)
+    for step in range(3):
+        tok = int(rng.integers(0, cfg.vocab))
+        g = m.forward(pool, [dict(tokens=[tok], start_pos=pos, block_table=table)], nmx.OUT_LOGITS_LAST)
+        check_logits(g, om.forward(cache, [tok], pos))
+        pos += 1

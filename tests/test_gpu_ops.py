@@ -126,6 +126,26 @@ def test_qmatmul_records(env, M, N, K):
         assert O.max_rel_err(got[m], ref[m]) <= 2e-3, (m, M)
 
 
+@pytest.mark.parametrize("M,N,K", [(64, 256, 512), (128, 512, 1024), (200, 768, 512), (333, 256, 2048),
+                                   (130, 4096, 4096)])
+def test_qmatmul_records_tensor_core_gemm(env, M, N, K):
+    """Many rows go through the tcgen05 GEMM (weights dequantised to f16 in
+    shared memory, f32 accumulation in TMEM): equals the oracle, ragged M."""
+    torch, nmx, ctx = env
+    rng = np.random.default_rng(M + 3 * N + K)
+    w = rng.standard_normal((N, K), dtype=np.float32) * 0.02
+    wq, s, b = O.quantize(w, 4, 64)
+    x = O.f32_to_f16bits(rng.standard_normal((M, K), dtype=np.float32))
+    ref = O.f16bits_to_f32(O.qmatmul(x, wq, s, b, 4, 64))
+    rec = ctx.pack_records(dev(torch, wq.view(np.int32)), u16(torch, s), u16(torch, b))
+    n0 = ctx.launches
+    y = ctx.quantized_matmul_records(u16(torch, x), rec, N)
+    got = O.f16bits_to_f32(host16(y))
+    assert ctx.launches - n0 == 1  # one GEMM launch for all rows
+    assert O.max_rel_err(got, ref) <= 2e-3, (M, N, K)
+    assert O.cosine(got.ravel(), ref.ravel()) > 0.99999
+
+
 @pytest.mark.parametrize("M,N,K", [(1, 6144, 4096), (1, 4096, 4096), (3, 5120, 1024), (1, 512, 640 // 128 * 128)])
 def test_qmatmul_records_deterministic(env, M, N, K):
     """Split tile groups are summed in a fixed order: repeated calls agree bit for bit."""
