@@ -4,20 +4,23 @@
 //
 // One CTA computes a 128 × 256 tile of the product (for SiLU·up: 128 rows
 // of gate and the matching 128 rows of up, one 128-column output tile) over
-// K in steps of 64 (one quantization group), through a ring of 4 shared
+// K in steps of 64 (one quantization group), through a ring of 3 shared
 // stages of {x tile 128 × 64, weight tile 256 × 64} f16, both K-major in the
 // 128-byte swizzle:
-//   * warp 5 loads the x tile with a TMA tensor copy (box 64 × 128,
+//   * warp 9 loads the x tile with a TMA tensor copy (box 64 × 128,
 //     SWIZZLE_128B; rows past M read as zeros);
-//   * warps 0-3 dequantize the weight tile straight from the records into
-//     the same swizzled layout: w = s·q + b rounded to f16 (the precision
+//   * warp 10 bulk-copies the 16 records of each 128-k block of the weight
+//     tile into a ring of 3 raw slots (cp.async.bulk, mbarrier tx count);
+//   * warps 0-7 dequantize the weight tile from the raw records into the
+//     same swizzled layout: w = s·q + b rounded to f16 (the precision
 //     MLX's own large-M kernel stages its weights in), with the nibble-to-
 //     f16 trick (q | 0x6400 = 1024 + q, minus 1024 exactly) and one f16 FMA;
-//   * one thread of warp 4 issues tcgen05.mma (kind::f16, M = 128, N = 256,
+//   * one thread of warp 8 issues tcgen05.mma (kind::f16, M = 128, N = 256,
 //     f32 accumulator in 256 TMEM columns) four times per stage and commits
 //     each stage back to its producers through an mbarrier;
-//   * after the last stage warps 0-3 read their 32 TMEM lanes each with
-//     tcgen05.ld (32x32b) and run the epilogue, one output row per thread.
+//   * after the last stage warps 0-7 read TMEM with tcgen05.ld (32x32b;
+//     warp w: lanes 32 (w % 4) .. +31, half the columns) and run the
+//     epilogue, one output row per thread.
 // All mbarrier waits are bounded; a wait that runs out sets bit 0 of *err
 // and the CTA skips ahead to its teardown (TMEM is always released).
 #include <cuda.h>
@@ -37,13 +40,17 @@ namespace {
 constexpr int kTM = 128;          // rows of x per CTA (MMA M)
 constexpr int kTN = 256;          // MMA N: weight rows per CTA
 constexpr int kTK = 64;           // k per stage (one group)
-constexpr int kTS = 4;            // stages
+constexpr int kTS = 3;            // stages
+constexpr int kRS = 3;            // raw record slots (one 128-k block of the 16 tiles each)
 constexpr int kABytes = kTM * kTK * 2;   // 16 KB
 constexpr int kBBytes = kTN * kTK * 2;   // 32 KB
 constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kGThreads = 192;    // warps 0-3 dequant + epilogue, 4 MMA, 5 TMA
+constexpr int kDW = 8;            // dequant / epilogue warps (one weight row per thread)
+constexpr int kGThreads = (kDW + 3) * 32;  // + MMA, x-tile and record-loader warps
+constexpr int kWMma = kDW, kWTma = kDW + 1, kWRec = kDW + 2;
 constexpr unsigned kGSpin = 1u << 24;
 constexpr int kRecG = 1152;
+constexpr int kRawBytes = 16 * kRecG;  // the 16 records of one block of the weight tile
 
 __device__ __forceinline__ unsigned sa_(const void* p) { return static_cast<unsigned>(__cvta_generic_to_shared(p)); }
 __device__ __forceinline__ void mbar_init(uint64_t* b, unsigned count) {
@@ -133,6 +140,8 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
   __shared__ __align__(8) uint64_t full[kTS];
   __shared__ __align__(8) uint64_t empty[kTS];
   __shared__ __align__(8) uint64_t acc_bar;
+  __shared__ __align__(8) uint64_t raw_full[kRS];
+  __shared__ __align__(8) uint64_t raw_empty[kRS];
   __shared__ uint32_t s_taddr;
   __shared__ int s_fail;
 
@@ -143,14 +152,18 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
 
   if (tid == 0) {
     for (int s = 0; s < kTS; ++s) {
-      mbar_init(&full[s], 1 + 128);  // TMA thread (expect_tx) + the 128 dequant threads
+      mbar_init(&full[s], 1 + kDW * 32);  // TMA thread (expect_tx) + the dequant threads
       mbar_init(&empty[s], 1);       // tcgen05.commit
     }
     mbar_init(&acc_bar, 1);
+    for (int s = 0; s < kRS; ++s) {
+      mbar_init(&raw_full[s], 1);      // record loader (expect_tx)
+      mbar_init(&raw_empty[s], kDW * 32);  // the dequant threads, after the block's second stage
+    }
     s_fail = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 4) {
+  if (warp == kWMma) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sa_(&s_taddr)), "r"(kTN)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -161,7 +174,34 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
   const uint32_t taddr = s_taddr;
   grid_wait();  // x (and the residual) come from the previous kernel
 
-  if (warp == 5) {
+  unsigned char* raw = smem + kTS * kStageBytes;
+  if (warp == kWRec) {
+    // ------------------------------------------- bulk copies: raw record blocks
+    if (lane == 0) {
+      for (int b = 0; b < nb; ++b) {
+        const int rs = b % kRS;
+        if (b >= kRS && !mbar_wait(&raw_empty[rs], ((b / kRS) - 1) & 1)) {
+          atomicOr(a.err, 1u);
+          s_fail = 1;
+          break;
+        }
+        mbar_expect_tx(&raw_full[rs], kRawBytes);
+        for (int i = 0; i < 16; ++i) {
+          long long T;  // 16-row tile of the matrix
+          if constexpr (EPI == EPI_SILU)
+            T = (i < 8) ? (long long)nt * 8 + i : a.pair_tiles + (long long)nt * 8 + (i - 8);
+          else
+            T = (long long)nt * 16 + i;
+          const unsigned char* src = a.w + (T * nb + b) * kRecG;
+          asm volatile(
+              "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                  sa_(raw + rs * kRawBytes + i * kRecG)),
+              "l"(src), "r"(kRecG), "r"(sa_(&raw_full[rs]))
+              : "memory");
+        }
+      }
+    }
+  } else if (warp == kWTma) {
     // ---------------------------------------------------------------- TMA: x tiles
     if (lane == 0) {
       for (int kt = 0; kt < KT; ++kt) {
@@ -180,7 +220,7 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
             : "memory");
       }
     }
-  } else if (warp == 4) {
+  } else if (warp == kWMma) {
     // ---------------------------------------------------------------- MMA issue
     if (lane == 0) {
       for (int kt = 0; kt < KT; ++kt) {
@@ -201,8 +241,8 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
       mma_commit(&acc_bar);
     }
   } else {
-    // ------------------------------------------- warps 0-3: dequantized weights
-    // thread t fills weight rows t and t + 128 of the tile
+    // ----------------------------------------- dequant warps: weight tile rows
+    // thread t fills weight row t of the tile
     for (int kt = 0; kt < KT; ++kt) {
       const int s = kt % kTS;
       if (kt >= kTS && !mbar_wait(&empty[s], ((kt / kTS) - 1) & 1)) {
@@ -211,22 +251,22 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
         break;
       }
       unsigned char* B = smem + s * kStageBytes + kABytes;
-      const int blk = kt >> 1, gi = kt & 1;
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        const int r = tid + 128 * h2;
-        long long n;  // weight row in the matrix
-        if constexpr (EPI == EPI_SILU)
-          n = (r < 128) ? (long long)nt * 128 + r : a.pair_tiles * 16 + (long long)nt * 128 + (r - 128);
-        else
-          n = (long long)nt * kTN + r;
-        const int g16 = int(n & 15), half_ = g16 >> 3, g = g16 & 7;
-        const unsigned char* rec = a.w + ((n >> 4) * nb + blk) * kRecG;
+      const int blk = kt >> 1, gi = kt & 1, rs = blk % kRS;
+      if (gi == 0 && !mbar_wait(&raw_full[rs], (blk / kRS) & 1)) {
+        atomicOr(a.err, 1u);
+        s_fail = 1;
+        break;
+      }
+      const unsigned char* rawb = raw + rs * kRawBytes;
+      {
+        const int r = tid;  // weight row of the tile: record r / 16, row r % 16
+        const int g16 = r & 15, half_ = g16 >> 3, g = g16 & 7;
+        const unsigned char* rec = rawb + (r >> 4) * kRecG;
         const unsigned char* wb = rec + half_ * 512 + 16 * (4 * g) + 8 * gi;
         // words 2t, 2t+1 of this group sit in lane 4g+t's 16 bytes
         uint2 wv[4];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) wv[t] = __ldg(reinterpret_cast<const uint2*>(wb + 16 * t));
+        for (int t = 0; t < 4; ++t) wv[t] = *reinterpret_cast<const uint2*>(wb + 16 * t);
         const __half sc = *reinterpret_cast<const __half*>(rec + 1024 + ((0 * 2 + gi) * 8 + g) * 4 + half_ * 2);
         const __half bi = *reinterpret_cast<const __half*>(rec + 1024 + ((1 * 2 + gi) * 8 + g) * 4 + half_ * 2);
         const __half2 s2 = __halves2half2(sc, sc);
@@ -255,6 +295,7 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
       // generic-proxy writes, read by the tensor core's async proxy
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_arrive(&full[s]);
+      if (gi == 1) mbar_arrive(&raw_empty[rs]);  // the block's records are read
     }
 
     // ------------------------------------------------------------ epilogue
@@ -263,10 +304,12 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
       s_fail = 1;
     }
     tc_fence_after();
-    const int m = m0 + 32 * warp + lane;
-    const uint32_t lane_addr = taddr + (uint32_t(32 * warp) << 16);
+    // warp w reads TMEM lanes 32 (w % 4) .. +31 (its rows) and half the columns
+    const int quad = warp & 3, chalf = warp >> 2;
+    const int m = m0 + 32 * quad + lane;
+    const uint32_t lane_addr = taddr + (uint32_t(32 * quad) << 16);
     constexpr int OUT = EPI == EPI_SILU ? 128 : kTN;  // output columns of the tile
-    for (int c0 = 0; c0 < OUT; c0 += 32) {
+    for (int c0 = chalf * (OUT / 2); c0 < (chalf + 1) * (OUT / 2); c0 += 32) {
       float v[32], u[32];
       tmem_ld32(lane_addr + c0, v);
       if constexpr (EPI == EPI_SILU) tmem_ld32(lane_addr + 128 + c0, u);
@@ -310,7 +353,7 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
   grid_launch_dependents();
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == kWMma) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(kTN) : "memory");
   }
@@ -333,7 +376,7 @@ template <int EPI>
 nmx_status_t launch_gemm(Ctx* c, const CUtensorMap& tm, const GemmArgs& g, dim3 grid) {
   static std::mutex mu;
   static std::map<int, bool> set;
-  const size_t smem = size_t(kTS) * kStageBytes + 1024;
+  const size_t smem = size_t(kTS) * kStageBytes + size_t(kRS) * kRawBytes + 1024;
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!set[c->device]) {
