@@ -391,6 +391,64 @@ NMX_API nmx_status_t nmx_block_pool_table_delete(nmx_block_pool_t pool, const ch
 NMX_API nmx_status_t nmx_block_pool_table_fork(nmx_block_pool_t pool, const char* src_request_id,
                                                const char* new_request_id);
 
+/* ------------------------------------------------------------------------ */
+/* Memory budget (MemoryBudgetTracker, Sources/NovaMLXEngine/MemoryBudgetTracker.swift):
+ * available = limit - weights - committed; canAdmit (:57-80) accepts
+ * estimated_tokens * bytes_per_token <= available * (100 - headroom) / 100;
+ * reserve / release per sequence id. */
+typedef struct nmx_budget_s* nmx_budget_t;
+NMX_API nmx_status_t nmx_budget_create(uint64_t limit_bytes, int headroom_percent, nmx_budget_t* out);
+NMX_API void nmx_budget_destroy(nmx_budget_t budget);
+NMX_API void nmx_budget_add_weights(nmx_budget_t budget, uint64_t bytes);
+NMX_API int nmx_budget_can_admit(nmx_budget_t budget, uint64_t estimated_tokens, uint64_t bytes_per_token);
+NMX_API void nmx_budget_reserve(nmx_budget_t budget, int64_t seq_id, uint64_t estimated_tokens,
+                                uint64_t bytes_per_token);
+NMX_API void nmx_budget_release(nmx_budget_t budget, int64_t seq_id);
+NMX_API uint64_t nmx_budget_available(nmx_budget_t budget);
+
+/* Continuous batching (FusedBatchScheduler's engine-step loop,
+ * Sources/NovaMLXEngine/FusedBatchScheduler.swift:281-1575): requests wait
+ * in submission order; a step admits what the concurrency limit
+ * (optimalConcurrency :264-277: sequences of 4096 tokens in 90% of the
+ * available budget, at most max_concurrent) and the budget (canAdmit,
+ * prompt + max_new_tokens tokens) allow, reusing cached prefix blocks, then
+ * runs ONE nmx_forward over every running sequence: a prefill chunk of up to
+ * prefill_chunk tokens for sequences still in their prompt, one decode token
+ * for the others, at most max_step_tokens tokens. When the page pool runs
+ * out, the newest other sequence is preempted (:502; its state becomes
+ * NMX_REQ_PREEMPTED and it must be submitted again). Greedy ids; a request
+ * ends after max_new_tokens ids or its eos id. The pool's blocks are the
+ * scheduler's to hand out; destroy the scheduler before the pool. */
+typedef struct {
+  int max_batch;           /* sequences per step (<= the model's max_batch) */
+  int max_step_tokens;     /* tokens per step (<= the model's max_tokens) */
+  int prefill_chunk;       /* prompt tokens per sequence per step (the reference: 512) */
+  int max_concurrent;      /* hard limit on running sequences */
+  int headroom_percent;    /* budget headroom (the reference: 10) */
+  uint64_t kv_budget_bytes; /* 0: the whole pool */
+  const char* model_name;  /* prefix-cache hash namespace (may be NULL) */
+} nmx_sched_cfg;
+enum { NMX_REQ_WAITING = 0, NMX_REQ_PREFILL = 1, NMX_REQ_DECODE = 2, NMX_REQ_DONE = 3, NMX_REQ_PREEMPTED = 4 };
+typedef struct {
+  uint64_t steps, generated, finished, preemptions, prefix_hit_tokens, tokens_in_steps;
+  int running, waiting;
+  int blocks_in_use;        /* distinct pool blocks held (shared prefix blocks once) */
+  uint64_t logical_blocks;  /* blocks summed over running sequences' tables */
+  uint64_t kv_available_bytes;
+} nmx_sched_stats_t;
+typedef struct nmx_sched_s* nmx_sched_t;
+NMX_API nmx_status_t nmx_sched_create(nmx_model_t model, nmx_kv_pool_t pool, const nmx_sched_cfg* cfg,
+                                      nmx_sched_t* out);
+NMX_API void nmx_sched_destroy(nmx_sched_t sched);
+NMX_API nmx_status_t nmx_sched_submit(nmx_sched_t sched, const int32_t* prompt, int n_tokens,
+                                      int max_new_tokens, int eos_id, int64_t* out_request_id);
+/* One engine step; *n_generated = ids produced by it. */
+NMX_API nmx_status_t nmx_sched_step(nmx_sched_t sched, int* n_generated);
+/* The request's ids so far (up to max_tokens copied) and its NMX_REQ_* state. */
+NMX_API nmx_status_t nmx_sched_poll(nmx_sched_t sched, int64_t request_id, int32_t* out_tokens,
+                                    int max_tokens, int* n_tokens, int* state);
+NMX_API nmx_status_t nmx_sched_stats(nmx_sched_t sched, nmx_sched_stats_t* out);
+
 #ifdef __cplusplus
 }
 #endif

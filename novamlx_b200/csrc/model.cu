@@ -19,6 +19,7 @@
 // the batched-decode shape of Sources/NovaMLXEngine/BatchScheduler.swift:162-258
 // (one forward for the whole batch), with KV in pages instead of padded,
 // stacked per-sequence caches (Sources/NovaMLXEngine/FusedBatchDecode.swift:95-147).
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -704,11 +705,12 @@ nmx_status_t Model::upload_batch(const nmx_seq_t* seqs, int n, int* T_out, bool*
   NMX_CUDA_OK(cudaMemcpyAsync(tok_seq, sq, size_t(T) * 4, cudaMemcpyHostToDevice, c->stream));
   NMX_CUDA_OK(cudaMemcpyAsync(tok_pos, ps, size_t(T) * 4, cudaMemcpyHostToDevice, c->stream));
   NMX_CUDA_OK(cudaMemcpyAsync(last_rows, last, size_t(n) * 4, cudaMemcpyHostToDevice, c->stream));
-  for (int i = 0; i < n; ++i)
-    NMX_CUDA_OK(cudaMemcpyAsync(block_tables + size_t(i) * kBlockCap, tbl + size_t(i) * kBlockCap,
-                                size_t(seqs[i].n_blocks) * 4, cudaMemcpyHostToDevice, c->stream));
-  h2d_bytes_last = size_t(T) * 12 + size_t(n) * 4;
-  for (int i = 0; i < n; ++i) h2d_bytes_last += size_t(seqs[i].n_blocks) * 4;
+  // all tables in one strided copy of the widest table's columns
+  int nb_max = 0;
+  for (int i = 0; i < n; ++i) nb_max = std::max(nb_max, seqs[i].n_blocks);
+  NMX_CUDA_OK(cudaMemcpy2DAsync(block_tables, size_t(kBlockCap) * 4, tbl, size_t(kBlockCap) * 4, size_t(nb_max) * 4,
+                                size_t(n), cudaMemcpyHostToDevice, c->stream));
+  h2d_bytes_last = size_t(T) * 12 + size_t(n) * 4 + size_t(n) * nb_max * 4;
   *T_out = T;
   *decode_out = decode;
   return NMX_OK;

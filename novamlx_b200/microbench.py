@@ -3,7 +3,8 @@
   python -m novamlx_b200.microbench gemv [--n 28672] [--k 4096] [--m 1]
   python -m novamlx_b200.microbench gemm [--m 2048] [--n 4096] [--k 4096]
   python -m novamlx_b200.microbench attn [--batch 1] [--ctx 2176]
-  python -m novamlx_b200.microbench decode [--layers 2] [--ctx 2048] [--tokens 64]
+  python -m novamlx_b200.microbench decode [--layers 2] [--ctx 2048] [--tokens 64] [--batch 1]
+  python -m novamlx_b200.microbench serve [--layers 32] [--seqs 64] [--tokens 256]
 
 gemv: the decode-record GEMV (nmx_op_qmatmul_records) over `copies` distinct
 weight copies, so the weights come from HBM on every launch.
@@ -13,10 +14,19 @@ attn: paged decode attention (nmx_op_attn_paged_decode) at Llama-3.1-8B
 head shapes (32 query heads, 8 KV heads, head dim 128, 16-token pages) over
 a pool larger than L2, each rep reading a different set of pages.
 
-decode: the model's batch-1 decode step (nmx_decode_greedy) on the
+decode: the model's decode step (nmx_decode_greedy, --batch sequences) on the
 Llama-3.1-8B architecture cut to --layers layers (random 4-bit weights), at
 context --ctx; the per-token time, and one short decode inside an NVTX range
 named "decode" for a profiler to select.
+
+serve: continuous batching (nmx_sched_*) on the Llama-3.1-8B architecture
+(random 4-bit weights, --layers layers): --seqs sequences, half of them a
+shared 2048-token random prefix plus a private suffix (total length uniform
+in [2064, 4096]), the others uniform in [512, 4096] tokens; each decodes
+--tokens greedy ids; 16-token pages, prefill chunks of 512. Reports the
+aggregate generated tok/s over the whole run, the tok/s of the steps where
+every running sequence decodes, the prefix-cache hit tokens, and the
+distinct vs logical KV pages at the widest decode step.
 
 Prints one JSON line per run with the average launch duration measured by
 CUDA events on the library's stream and the algorithmic bytes per launch.
@@ -57,17 +67,21 @@ def gemv(ctx, torch, n, k, m, copies, reps):
             "gbs": round(nbytes / us / 1e3, 1)}
 
 
-def gemm(ctx, torch, m, n, k, reps):
+def gemm(ctx, torch, m, n, k, reps, copies=1):
     wf = torch.randn((n, k), device="cuda", dtype=torch.float32) * 0.02
-    wq, s, b = ctx.quantize(wf, 64, 4)
-    rec = ctx.pack_records(wq, s, b)
-    del wf, wq, s, b
+    recs = []
+    for _ in range(copies):
+        wq, s, b = ctx.quantize(wf, 64, 4)
+        recs.append(ctx.pack_records(wq, s, b))
+        del wq, s, b
+    del wf
     x = torch.randn((m, k), device="cuda", dtype=torch.float16)
     y = torch.empty((m, n), device="cuda", dtype=torch.float16)
-    us = _time(torch, lambda i: ctx.quantized_matmul_records(x, rec, n, out=y), reps)
+    us = _time(torch, lambda i: ctx.quantized_matmul_records(x, recs[i % copies], n, out=y), reps)
     flops = 2.0 * m * n * k
-    return {"kernel": "qgemm_tc_kernel", "m": m, "n": n, "k": k, "us": round(us, 2),
-            "tflops": round(flops / us / 1e6, 1)}
+    wbytes = n * k // 2 + 2 * n * (k // 64) * 2
+    return {"kernel": "qgemm_tc_kernel", "m": m, "n": n, "k": k, "copies": copies, "us": round(us, 2),
+            "tflops": round(flops / us / 1e6, 1), "weight_gbs": round(wbytes / us / 1e3, 1)}
 
 
 def attn(ctx, torch, batch, ctx_len, reps, hq=32, hkv=8, d=128, bt=16):
@@ -88,35 +102,96 @@ def attn(ctx, torch, batch, ctx_len, reps, hq=32, hkv=8, d=128, bt=16):
             "bytes": nbytes, "gbs": round(nbytes / us / 1e3, 1)}
 
 
-def decode(ctx, torch, nmx, layers, ctx_len, tokens):
+def decode(ctx, torch, nmx, layers, ctx_len, tokens, batch=1):
     import numpy as np
-    cfg = nmx.llama31_8b(n_layers=layers, max_batch=1, max_tokens=ctx_len)
+    cfg = nmx.llama31_8b(n_layers=layers, max_batch=batch, max_tokens=max(ctx_len, batch))
     m = nmx.Model(ctx, cfg)
     m.init_random(seed=0, std=0.02)
     nblk = (ctx_len + tokens + 15) // 16 + 1
-    pool = nmx.KVPool(m, nblk + 4)
-    table = np.arange(nblk, dtype=np.int32)
-    prompt = np.random.default_rng(0).integers(0, cfg.vocab, ctx_len)
-    first = int(m.forward(pool, [dict(tokens=prompt, start_pos=0, block_table=table)])[0])
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    m.forward(pool, [dict(tokens=prompt, start_pos=0, block_table=table)])
-    prefill_ms = (time.perf_counter() - t0) * 1000.0
+    pool = nmx.KVPool(m, batch * nblk + 4)
+    tables = np.arange(batch * nblk, dtype=np.int32).reshape(batch, nblk)
+    rng = np.random.default_rng(0)
+    prompts = [rng.integers(0, cfg.vocab, ctx_len) for _ in range(batch)]
+    first = []
+    prefill_ms = 0.0
+    for b in range(batch):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        first.append(int(m.forward(pool, [dict(tokens=prompts[b], start_pos=0, block_table=tables[b])])[0]))
+        prefill_ms = (time.perf_counter() - t0) * 1000.0
     for _ in range(3):
-        m.decode_greedy(pool, [first], [ctx_len], table[None], 8, want_ids=False)
+        m.decode_greedy(pool, first, [ctx_len] * batch, tables, 8, want_ids=False)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    m.decode_greedy(pool, [first], [ctx_len], table[None], tokens, want_ids=False)
+    m.decode_greedy(pool, first, [ctx_len] * batch, tables, tokens, want_ids=False)
     e1.record()
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1000.0 / tokens
     torch.cuda.nvtx.range_push("decode")
-    m.decode_greedy(pool, [first], [ctx_len], table[None], 2, want_ids=False)
+    m.decode_greedy(pool, first, [ctx_len] * batch, tables, 2, want_ids=False)
     torch.cuda.synchronize()
     torch.cuda.nvtx.range_pop()
-    return {"what": "decode step", "layers": layers, "ctx": ctx_len, "us_per_token": round(us, 2),
-            "prefill_ms": round(prefill_ms, 2), "weight_bytes_per_token": m.step_weight_bytes}
+    return {"what": "decode step", "layers": layers, "batch": batch, "ctx": ctx_len, "us_per_step": round(us, 2),
+            "tok_s": round(batch * 1e6 / us, 1), "prefill_ms": round(prefill_ms, 2),
+            "weight_bytes_per_step": m.step_weight_bytes}
+
+
+def serve(ctx, torch, nmx, layers, n_seqs, tokens, step_tokens, chunk, seed=0):
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    prefix = rng.integers(0, 128256, 2048)
+    prompts = []
+    for i in range(n_seqs):
+        if i % 2 == 0:
+            total = int(rng.integers(2064, 4097))
+            prompts.append(np.concatenate([prefix, rng.integers(0, 128256, total - 2048)]))
+        else:
+            prompts.append(rng.integers(0, 128256, int(rng.integers(512, 4097))))
+    cfg = nmx.llama31_8b(n_layers=layers, max_batch=n_seqs, max_tokens=step_tokens)
+    m = nmx.Model(ctx, cfg)
+    m.init_random(seed=0, std=0.02)
+    bpt = m.kv_bytes_per_token
+    logical_blocks = sum((len(p) + tokens + 15) // 16 for p in prompts)
+    pool = nmx.KVPool(m, logical_blocks + 8)  # room for every page unshared: no preemption
+    sched = nmx.Scheduler(m, pool, max_batch=n_seqs, max_step_tokens=step_tokens, prefill_chunk=chunk,
+                          max_concurrent=n_seqs, kv_budget_bytes=160 << 30, model_name="llama-3.1-8b")
+    ids = [sched.submit(p, tokens) for p in prompts]
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    dec_t = dec_tok = 0.0
+    widest = (0, 0, 0)
+    steps = 0
+    while True:
+        st0 = sched.stats()
+        if st0["finished"] == n_seqs:
+            break
+        s0 = time.perf_counter()
+        gen = sched.step()
+        dt = time.perf_counter() - s0
+        st = sched.stats()
+        steps += 1
+        if gen > 0 and st["tokens_in_steps"] - st0["tokens_in_steps"] == gen:  # every row a decode row
+            dec_t += dt
+            dec_tok += gen
+            if gen > widest[0]:
+                widest = (gen, st["blocks_in_use"], st["logical_blocks"])
+        if steps > 100000:
+            raise RuntimeError("scheduler did not drain")
+    wall = time.perf_counter() - t0
+    st = sched.stats()
+    gen_total = st["generated"]
+    assert all(len(sched.poll(r)[0]) == tokens for r in ids)
+    sched.close()
+    return {"what": "continuous batching", "layers": layers, "seqs": n_seqs, "tokens_each": tokens,
+            "prompt_tokens": int(sum(len(p) for p in prompts)), "steps": st["steps"],
+            "wall_s": round(wall, 3), "tok_s": round(gen_total / wall, 1),
+            "decode_steps_tok_s": round(dec_tok / dec_t, 1) if dec_t else None,
+            "prefix_hit_tokens": st["prefix_hit_tokens"], "tokens_in_steps": st["tokens_in_steps"],
+            "widest_decode_step": {"seqs": widest[0], "distinct_pages": widest[1], "logical_pages": widest[2],
+                                   "distinct_kv_gb": round(widest[1] * 16 * bpt / 1e9, 2),
+                                   "logical_kv_gb": round(widest[2] * 16 * bpt / 1e9, 2)},
+            "kv_bytes_per_token": bpt, "weight_bytes_per_step": m.step_weight_bytes}
 
 
 def main():
@@ -125,17 +200,26 @@ def main():
     from novamlx_b200 import nmx
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemv", "gemm", "attn", "decode"])
+    ap.add_argument("what", choices=["gemv", "gemm", "attn", "decode", "serve"])
     ap.add_argument("--n", type=int, default=None, help="gemv: 28672, gemm: 4096")
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--m", type=int, default=None, help="gemv: 1, gemm: 2048")
-    ap.add_argument("--copies", type=int, default=3)
+    ap.add_argument("--copies", type=int, default=None, help="gemv: 3, gemm: 1")
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--reps", type=int, default=30)
-    ap.add_argument("--layers", type=int, default=2)
-    ap.add_argument("--tokens", type=int, default=64)
+    ap.add_argument("--layers", type=int, default=None, help="decode: 2, serve: 32")
+    ap.add_argument("--tokens", type=int, default=None, help="decode: 64, serve: 256")
+    ap.add_argument("--seqs", type=int, default=64)
+    ap.add_argument("--step-tokens", type=int, default=4096)
+    ap.add_argument("--chunk", type=int, default=512)
     a = ap.parse_args()
+    if a.copies is None:
+        a.copies = 1 if a.what == "gemm" else 3
+    if a.layers is None:
+        a.layers = 32 if a.what == "serve" else 2
+    if a.tokens is None:
+        a.tokens = 256 if a.what == "serve" else 64
     if a.n is None:
         a.n = 4096 if a.what == "gemm" else 28672
     if a.m is None:
@@ -146,11 +230,13 @@ def main():
         if a.what == "gemv":
             r = gemv(c, torch, a.n, a.k, a.m, a.copies, a.reps)
         elif a.what == "gemm":
-            r = gemm(c, torch, a.m, a.n, a.k, a.reps)
+            r = gemm(c, torch, a.m, a.n, a.k, a.reps, a.copies)
         elif a.what == "attn":
             r = attn(c, torch, a.batch, a.ctx, a.reps)
+        elif a.what == "serve":
+            r = serve(c, torch, nmx, a.layers, a.seqs, a.tokens, a.step_tokens, a.chunk)
         else:
-            r = decode(c, torch, nmx, a.layers, a.ctx, a.tokens)
+            r = decode(c, torch, nmx, a.layers, a.ctx, a.tokens, a.batch)
     print(json.dumps(r), flush=True)
 
 

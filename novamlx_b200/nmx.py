@@ -110,6 +110,35 @@ _proto("nmx_decode_greedy", _i, _vp, _vp, _ip, _ip, _ip, _i, _i, _i, _ip)
 _proto("nmx_block_hash", None, _u8p, _ip, _i, C.c_char_p, _u8p)
 _proto("nmx_chain_hashes", _i, _ip, _i, _i, C.c_char_p, _u8p, _i)
 _proto("nmx_block_pool_create", _i, _i, _i, _i, C.c_char_p, C.POINTER(_vp))
+
+
+class SchedCfg(C.Structure):
+    _fields_ = [("max_batch", C.c_int), ("max_step_tokens", C.c_int), ("prefill_chunk", C.c_int),
+                ("max_concurrent", C.c_int), ("headroom_percent", C.c_int), ("kv_budget_bytes", C.c_uint64),
+                ("model_name", C.c_char_p)]
+
+
+class SchedStats(C.Structure):
+    _fields_ = [("steps", C.c_uint64), ("generated", C.c_uint64), ("finished", C.c_uint64),
+                ("preemptions", C.c_uint64), ("prefix_hit_tokens", C.c_uint64), ("tokens_in_steps", C.c_uint64),
+                ("running", C.c_int), ("waiting", C.c_int), ("blocks_in_use", C.c_int),
+                ("logical_blocks", C.c_uint64), ("kv_available_bytes", C.c_uint64)]
+
+
+_proto("nmx_budget_create", _i, C.c_uint64, _i, C.POINTER(_vp))
+_proto("nmx_budget_destroy", None, _vp)
+_proto("nmx_budget_add_weights", None, _vp, C.c_uint64)
+_proto("nmx_budget_can_admit", _i, _vp, C.c_uint64, C.c_uint64)
+_proto("nmx_budget_reserve", None, _vp, C.c_int64, C.c_uint64, C.c_uint64)
+_proto("nmx_budget_release", None, _vp, C.c_int64)
+_proto("nmx_budget_available", C.c_uint64, _vp)
+_proto("nmx_sched_create", _i, _vp, _vp, C.POINTER(SchedCfg), C.POINTER(_vp))
+_proto("nmx_sched_destroy", None, _vp)
+_proto("nmx_sched_submit", _i, _vp, _vp, _i, _i, _i, C.POINTER(C.c_int64))
+_proto("nmx_sched_step", _i, _vp, C.POINTER(C.c_int))
+_proto("nmx_sched_poll", _i, _vp, C.c_int64, _vp, _i, C.POINTER(C.c_int), C.POINTER(C.c_int))
+_proto("nmx_sched_stats", _i, _vp, C.POINTER(SchedStats))
+REQ_WAITING, REQ_PREFILL, REQ_DECODE, REQ_DONE, REQ_PREEMPTED = range(5)
 _proto("nmx_block_pool_destroy", None, _vp)
 _proto("nmx_block_pool_allocate", _i, _vp)
 _proto("nmx_block_pool_free", None, _vp, _i)
@@ -632,3 +661,84 @@ class PagedBlockPool:
 
     def fork_block_table(self, source_request_id: str, new_request_id: str):
         check(lib.nmx_block_pool_table_fork(self.h, source_request_id.encode(), new_request_id.encode()))
+
+
+class MemoryBudget:
+    """nmx_budget_t: MemoryBudgetTracker's admission arithmetic (10% headroom by default)."""
+
+    def __init__(self, limit_bytes: int, headroom_percent: int = 10):
+        h = _vp()
+        check(lib.nmx_budget_create(limit_bytes, headroom_percent, C.byref(h)))
+        self.h = h
+
+    def add_weights(self, nbytes: int):
+        lib.nmx_budget_add_weights(self.h, nbytes)
+
+    def can_admit(self, estimated_tokens: int, bytes_per_token: int) -> bool:
+        return bool(lib.nmx_budget_can_admit(self.h, estimated_tokens, bytes_per_token))
+
+    def reserve(self, seq_id: int, estimated_tokens: int, bytes_per_token: int):
+        lib.nmx_budget_reserve(self.h, seq_id, estimated_tokens, bytes_per_token)
+
+    def release(self, seq_id: int):
+        lib.nmx_budget_release(self.h, seq_id)
+
+    @property
+    def available(self) -> int:
+        return int(lib.nmx_budget_available(self.h))
+
+    def __del__(self, _finalizing=sys.is_finalizing):
+        if not _finalizing() and getattr(self, "h", None):
+            lib.nmx_budget_destroy(self.h)
+            self.h = None
+
+
+class Scheduler:
+    """nmx_sched_t: continuous batching (admission, prefix reuse, chunked prefill,
+    one batched forward per step, preemption of the newest sequence)."""
+
+    def __init__(self, model: Model, pool: KVPool, max_batch: int, max_step_tokens: int, prefill_chunk: int = 512,
+                 max_concurrent: int = 64, headroom_percent: int = 10, kv_budget_bytes: int = 0,
+                 model_name: str = ""):
+        self._name = model_name.encode()
+        cfg = SchedCfg(max_batch, max_step_tokens, prefill_chunk, max_concurrent, headroom_percent, kv_budget_bytes,
+                       self._name)
+        h = _vp()
+        check(lib.nmx_sched_create(model.h, pool.h, C.byref(cfg), C.byref(h)))
+        self.h = h
+        self.model = model
+        self.pool = pool  # the scheduler hands out this pool's blocks: keep it alive
+
+    def submit(self, prompt, max_new_tokens: int, eos_id: int = -1) -> int:
+        p = _i32(prompt)
+        rid = C.c_int64()
+        check(lib.nmx_sched_submit(self.h, _iptr(p), len(p), max_new_tokens, eos_id, C.byref(rid)))
+        return int(rid.value)
+
+    def step(self) -> int:
+        n = C.c_int()
+        check(lib.nmx_sched_step(self.h, C.byref(n)))
+        return int(n.value)
+
+    def poll(self, rid: int):
+        n, st = C.c_int(), C.c_int()
+        check(lib.nmx_sched_poll(self.h, rid, None, 0, C.byref(n), C.byref(st)))
+        out = np.empty(n.value, np.int32)
+        if n.value:
+            check(lib.nmx_sched_poll(self.h, rid, out.ctypes.data, n.value, C.byref(n), C.byref(st)))
+        return out, int(st.value)
+
+    def stats(self) -> dict:
+        st = SchedStats()
+        check(lib.nmx_sched_stats(self.h, C.byref(st)))
+        return {f: getattr(st, f) for f, _ in SchedStats._fields_}
+
+    def close(self):
+        if self.h:
+            lib.nmx_sched_destroy(self.h)
+            self.h = None
+
+    def __del__(self, _finalizing=sys.is_finalizing):
+        if _finalizing():
+            return
+        self.close()
