@@ -217,7 +217,8 @@ NMX_API nmx_status_t nmx_op_qmatmul_records(nmx_ctx_t ctx, const void* x, const 
   NMX_CHECK(reinterpret_cast<uintptr_t>(records) % 16 == 0, NMX_ERR_INVALID, "records must be 16-byte aligned");
   Ctx* c = &ctx->c;
   GemvDLArgs a;
-  const size_t pf = qgemv_dl_partials_floats(N, K, EPI_STORE, c->num_sms, a.ctas_per_sm);
+  const size_t pf = std::max(qgemv_dl_partials_floats(N, K, EPI_STORE, c->num_sms, a.ctas_per_sm),
+                             qgemm_tcs_partials_floats(std::min(M, kTcsMaxRows), N, K, EPI_STORE, c->num_sms));
   void* ws = nullptr;
   NMX_TRY(ctx_workspace(c, pf * 4 + 256, &ws));
   unsigned* ctr = nullptr;

@@ -9,8 +9,9 @@
 // 128-byte swizzle:
 //   * warp 9 loads the x tile with a TMA tensor copy (box 64 × 128,
 //     SWIZZLE_128B; rows past M read as zeros);
-//   * warp 10 bulk-copies the 16 records of each 128-k block of the weight
-//     tile into a ring of 3 raw slots (cp.async.bulk, mbarrier tx count);
+//   * warp 10 brings the 16 records of each 128-k block of the weight tile
+//     into a ring of 3 raw slots with two 3-d tensor copies of 8 records
+//     (mbarrier tx count);
 //   * warps 0-7 dequantize the weight tile from the raw records into the
 //     same swizzled layout: w = s·q + b rounded to f16 (the precision
 //     MLX's own large-M kernel stages its weights in), with the nibble-to-
@@ -23,15 +24,12 @@
 //     epilogue, one output row per thread.
 // All mbarrier waits are bounded; a wait that runs out sets bit 0 of *err
 // and the CTA skips ahead to its teardown (TMEM is always released).
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
 #include <map>
 #include <mutex>
 
 #include "common.cuh"
 #include "kernels.h"
-#include "qgemv_common.cuh"
+#include "tc_common.cuh"
 
 namespace nmx {
 
@@ -48,76 +46,21 @@ constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kDW = 8;            // dequant / epilogue warps (one weight row per thread)
 constexpr int kGThreads = (kDW + 3) * 32;  // + MMA, x-tile and record-loader warps
 constexpr int kWMma = kDW, kWTma = kDW + 1, kWRec = kDW + 2;
-constexpr unsigned kGSpin = 1u << 24;
-constexpr int kRecG = 1152;
-constexpr int kRawBytes = 16 * kRecG;  // the 16 records of one block of the weight tile
-
-__device__ __forceinline__ unsigned sa_(const void* p) { return static_cast<unsigned>(__cvta_generic_to_shared(p)); }
-__device__ __forceinline__ void mbar_init(uint64_t* b, unsigned count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sa_(b)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sa_(b)) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sa_(b)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity) {
-  const unsigned a = sa_(b);
-  for (unsigned it = 0; it < kGSpin; ++it) {
-    unsigned ok;
-    asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-        : "=r"(ok)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (ok) return true;
-  }
-  return false;
-}
-
-// K-major operand in the 128-byte swizzle: 8-row groups 1024 B apart (SBO),
-// version 1, layout SWIZZLE_128B (2); the start address steps 32 B per k16
-__device__ __forceinline__ uint64_t smem_desc(const void* p) {
-  const uint64_t a = sa_(p);
-  return ((a >> 4) & 0x3FFFull) | (1ull << 16) | (uint64_t(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
-}
-// kind::f16 instruction descriptor: f32 accumulator, f16 A and B, both K-major
-constexpr uint32_t kIDesc = (1u << 4) | (uint32_t(kTN >> 3) << 17) | (uint32_t(kTM >> 4) << 24);
-
+constexpr int kRawBytes = 16 * tc::kRecPad;  // the 16 records of one block of the weight tile (two boxes of 8)
+constexpr int kRecG = tc::kRecG;
+constexpr uint32_t kIDesc = tc::idesc_f16(kTM, kTN);
+using tc::mbar_init;
+using tc::mbar_arrive;
+using tc::mbar_expect_tx;
+using tc::mbar_wait;
+using tc::sa_;
+using tc::smem_desc;
+using tc::mma_commit;
+using tc::tc_fence_after;
+using tc::tc_fence_before;
+using tc::tmem_ld32;
 __device__ __forceinline__ void mma_f16_tc(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-  asm volatile(
-      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIDesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(sa_(bar))
-               : "memory");
-}
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-
-// 32 consecutive f32 columns of this thread's TMEM lane
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// byte offset of (row, 16-byte chunk) in a K-major 64-wide f16 tile, 128 B swizzle
-__device__ __forceinline__ int sw128(int row, int chunk) {
-  return (row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4);
+  tc::mma_f16(tmem_d, adesc, bdesc, kIDesc, accumulate);
 }
 
 struct GemmArgs {
@@ -134,9 +77,12 @@ struct GemmArgs {
 
 template <int EPI>
 __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                                                 const __grid_constant__ CUtensorMap tmap_w,
                                                                  GemmArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned, derived from the shared array itself so that its
+  // loads and stores compile to shared-memory (not generic) accesses
+  unsigned char* smem = smem_raw + ((1024u - (tc::sa_(smem_raw) & 1023u)) & 1023u);
   __shared__ __align__(8) uint64_t full[kTS];
   __shared__ __align__(8) uint64_t empty[kTS];
   __shared__ __align__(8) uint64_t acc_bar;
@@ -186,18 +132,15 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
           break;
         }
         mbar_expect_tx(&raw_full[rs], kRawBytes);
-        for (int i = 0; i < 16; ++i) {
-          long long T;  // 16-row tile of the matrix
+        // two tensor copies of 8 consecutive 16-row tiles each
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          long long T0;
           if constexpr (EPI == EPI_SILU)
-            T = (i < 8) ? (long long)nt * 8 + i : a.pair_tiles + (long long)nt * 8 + (i - 8);
+            T0 = h == 0 ? (long long)nt * 8 : a.pair_tiles + (long long)nt * 8;
           else
-            T = (long long)nt * 16 + i;
-          const unsigned char* src = a.w + (T * nb + b) * kRecG;
-          asm volatile(
-              "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                  sa_(raw + rs * kRawBytes + i * kRecG)),
-              "l"(src), "r"(kRecG), "r"(sa_(&raw_full[rs]))
-              : "memory");
+            T0 = (long long)nt * 16 + 8 * h;
+          tc::load_records(raw + rs * kRawBytes + h * 8 * tc::kRecPad, &tmap_w, b, int(T0), &raw_full[rs]);
         }
       }
     }
@@ -223,6 +166,10 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
   } else if (warp == kWMma) {
     // ---------------------------------------------------------------- MMA issue
     if (lane == 0) {
+      // one thread issues every MMA: descriptors are computed once and
+      // advanced with adds (start addresses in 16-byte units)
+      const uint64_t desc0 = smem_desc(smem);
+      constexpr uint32_t kStageD = kStageBytes >> 4, kAD = kABytes >> 4;
       for (int kt = 0; kt < KT; ++kt) {
         const int s = kt % kTS;
         if (!mbar_wait(&full[s], (kt / kTS) & 1)) {
@@ -231,18 +178,17 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
           break;
         }
         tc_fence_after();
-        unsigned char* A = smem + s * kStageBytes;
-        unsigned char* B = A + kABytes;
+        const uint64_t ad = desc0 + uint64_t(s * kStageD), bd = ad + kAD;
+        const uint32_t first = kt ? 1u : 0u;
 #pragma unroll
         for (int k16 = 0; k16 < kTK / 16; ++k16)
-          mma_f16_tc(taddr, smem_desc(A + 32 * k16), smem_desc(B + 32 * k16), (kt | k16) ? 1u : 0u);
+          mma_f16_tc(taddr, ad + 2 * k16, bd + 2 * k16, k16 ? 1u : first);
         mma_commit(&empty[s]);
       }
       mma_commit(&acc_bar);
     }
   } else {
     // ----------------------------------------- dequant warps: weight tile rows
-    // thread t fills weight row t of the tile
     for (int kt = 0; kt < KT; ++kt) {
       const int s = kt % kTS;
       if (kt >= kTS && !mbar_wait(&empty[s], ((kt / kTS) - 1) & 1)) {
@@ -258,40 +204,8 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
         break;
       }
       const unsigned char* rawb = raw + rs * kRawBytes;
-      {
-        const int r = tid;  // weight row of the tile: record r / 16, row r % 16
-        const int g16 = r & 15, half_ = g16 >> 3, g = g16 & 7;
-        const unsigned char* rec = rawb + (r >> 4) * kRecG;
-        const unsigned char* wb = rec + half_ * 512 + 16 * (4 * g) + 8 * gi;
-        // words 2t, 2t+1 of this group sit in lane 4g+t's 16 bytes
-        uint2 wv[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) wv[t] = *reinterpret_cast<const uint2*>(wb + 16 * t);
-        const __half sc = *reinterpret_cast<const __half*>(rec + 1024 + ((0 * 2 + gi) * 8 + g) * 4 + half_ * 2);
-        const __half bi = *reinterpret_cast<const __half*>(rec + 1024 + ((1 * 2 + gi) * 8 + g) * 4 + half_ * 2);
-        const __half2 s2 = __halves2half2(sc, sc);
-        const __half2 s16 = __hmul2(s2, __float2half2_rn(0.0625f));
-        const __half2 b2 = __halves2half2(bi, bi);
-        const __half2 k1024 = __float2half2_rn(1024.f);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t word = (j & 1) ? wv[j >> 1].y : wv[j >> 1].x;
-          uint32_t P[4];
-          dequant_word<4>(word, P);  // (q0,q4), (16q1,16q5), (q2,q6), (16q3,16q7), each + 1024
-          __half2 v0 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&P[0]), k1024), s2, b2);   // w0, w4
-          __half2 v1 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&P[1]), k1024), s16, b2);  // w1, w5
-          __half2 v2 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&P[2]), k1024), s2, b2);   // w2, w6
-          __half2 v3 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&P[3]), k1024), s16, b2);  // w3, w7
-          const uint32_t u0 = *reinterpret_cast<uint32_t*>(&v0), u1 = *reinterpret_cast<uint32_t*>(&v1);
-          const uint32_t u2 = *reinterpret_cast<uint32_t*>(&v2), u3 = *reinterpret_cast<uint32_t*>(&v3);
-          uint4 o;
-          o.x = __byte_perm(u0, u1, 0x5410);  // w0, w1
-          o.y = __byte_perm(u2, u3, 0x5410);  // w2, w3
-          o.z = __byte_perm(u0, u1, 0x7632);  // w4, w5
-          o.w = __byte_perm(u2, u3, 0x7632);  // w6, w7
-          *reinterpret_cast<uint4*>(B + sw128(r, j)) = o;
-        }
-      }
+      // thread t fills weight row t of the tile: record t / 16, row t % 16
+      tc::dequant_record_row(rawb + (tid >> 4) * tc::kRecPad, tid & 15, gi, B, tid);
       // generic-proxy writes, read by the tensor core's async proxy
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_arrive(&full[s]);
@@ -359,21 +273,8 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
   }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, []() {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
 template <int EPI>
-nmx_status_t launch_gemm(Ctx* c, const CUtensorMap& tm, const GemmArgs& g, dim3 grid) {
+nmx_status_t launch_gemm(Ctx* c, const CUtensorMap& tm, const CUtensorMap& tw, const GemmArgs& g, dim3 grid) {
   static std::mutex mu;
   static std::map<int, bool> set;
   const size_t smem = size_t(kTS) * kStageBytes + size_t(kRS) * kRawBytes + 1024;
@@ -384,7 +285,7 @@ nmx_status_t launch_gemm(Ctx* c, const CUtensorMap& tm, const GemmArgs& g, dim3 
       set[c->device] = true;
     }
   }
-  return launch(c, qgemm_tc_kernel<EPI>, grid, dim3(kGThreads), smem, tm, g);
+  return launch(c, qgemm_tc_kernel<EPI>, grid, dim3(kGThreads), smem, tm, tw, g);
 }
 
 }  // namespace
@@ -405,19 +306,11 @@ nmx_status_t qgemm_tc(Ctx* c, const GemvDLArgs& a, int epi) {
   NMX_CHECK(reinterpret_cast<uintptr_t>(a.y) % 16 == 0 && (a.ldy * 2) % 16 == 0 &&
                 (!a.res || (reinterpret_cast<uintptr_t>(a.res) % 16 == 0 && (a.ldres * 2) % 16 == 0)),
             NMX_ERR_UNSUPPORTED, "qgemm_tc: y / residual must be 16-byte aligned");
-  auto enc = tensor_map_encoder();
-  NMX_CHECK(enc != nullptr, NMX_ERR_UNSUPPORTED, "qgemm_tc: no tensor-map encoder in the driver");
   if (a.M == 0) return NMX_OK;
-  // x as a [M rows][K cols] f16 tensor; box 64 (k) × 128 (rows), 128-byte swizzle
-  CUtensorMap tm;
-  const cuuint64_t dims[2] = {cuuint64_t(a.K), cuuint64_t(a.M)};
-  const cuuint64_t strides[1] = {cuuint64_t(a.ldx) * 2};
-  const cuuint32_t box[2] = {cuuint32_t(kTK), cuuint32_t(kTM)};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a.x), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  NMX_CHECK(r == CUDA_SUCCESS, NMX_ERR_CUDA, "qgemm_tc: cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+  CUtensorMap tm, tw;
+  NMX_TRY(tc::encode_x_map(&tm, a.x, a.ldx, a.M, a.K, kTM));
+  const long long rows = epi == EPI_SILU ? (long long)a.pair_tiles * 16 + a.N : a.N;
+  NMX_TRY(tc::encode_records_map(&tw, a.w, a.K / 128, rows / 16, 8));
   GemmArgs g;
   g.w = static_cast<const unsigned char*>(a.w);
   g.M = a.M;
@@ -434,9 +327,9 @@ nmx_status_t qgemm_tc(Ctx* c, const GemvDLArgs& a, int epi) {
   const int ntiles = epi == EPI_SILU ? a.N / 128 : a.N / kTN;
   const dim3 grid(mt, ntiles);
   switch (epi) {
-    case EPI_STORE: return launch_gemm<EPI_STORE>(c, tm, g, grid);
-    case EPI_RESID: return launch_gemm<EPI_RESID>(c, tm, g, grid);
-    default: return launch_gemm<EPI_SILU>(c, tm, g, grid);
+    case EPI_STORE: return launch_gemm<EPI_STORE>(c, tm, tw, g, grid);
+    case EPI_RESID: return launch_gemm<EPI_RESID>(c, tm, tw, g, grid);
+    default: return launch_gemm<EPI_SILU>(c, tm, tw, g, grid);
   }
 }
 

@@ -1,0 +1,588 @@
+// Decode-batch GEMM on the 5th-generation tensor cores: y[M, N] = x[M, K] ·
+// dequant(W)[N, K]ᵀ for 1..128 activation rows (a continuous-batching decode
+// step, a speculative verify block), W in decode records (4-bit, group 64).
+//
+// At these row counts the product is bound by the weight stream, so the
+// tile is turned around: 128 WEIGHT rows are the MMA's M (TMEM lanes) and
+// the activation rows, rounded up to a multiple of 16 (NT), are its N
+// (TMEM columns). A CTA owns a group of tg such weight tiles (for SiLU·up,
+// gate/up pairs: both halves of an output tile sit in one TMEM lane) and a
+// contiguous share of the K blocks (128 k); the grid is (groups × S
+// K-shares), sized by the host to one wave over the SMs. Per K block:
+//   * warp 18 brings the 8 records of each of the group's tiles into a ring
+//     of raw slots with ONE 3-d tensor copy per tile (a copy per record
+//     costs more issue time than its bytes take to arrive); these are
+//     weights, so the copies may start before the programmatic-launch wait;
+//   * warp 17 loads the block's x tile once for the whole group (two TMA
+//     boxes of 64 k × NT rows, SWIZZLE_128B, rows past M read as zeros);
+//   * four warpgroups (warps 0-15) take the (block, tile) units in turn:
+//     each thread reads one weight row of the unit (64 bytes, conflict-free:
+//     see lane_row) and writes its 128 f16 weights w = s·q + b straight into
+//     its TMEM lane with tcgen05.st, into one of four 64-column A stages, so
+//     the dequantized tile never touches shared memory;
+//   * one thread of warp 16 issues eight tcgen05.mma (A from TMEM, x from
+//     shared memory; M = 128, N = NT, K = 16) per unit into that tile's
+//     accumulator (TMEM columns tile·NT ...), committing the A stage (and
+//     after the group's last tile the x tile) back to its producers.
+// After the last block warps 0-15 read the accumulators (tcgen05.ld 32x32b;
+// warp w: lanes 32 (w % 4) .., every fourth 8-column chunk). With one K share they run
+// the epilogue directly; with S shares each CTA stores its f32 partial
+// tiles, bumps the group's counter and waits (bounded) until all S have
+// (the grid is a single wave of one CTA per SM, so they are resident or
+// done); then each CTA sums its slice of the group's outputs over the S
+// partials in share order (deterministic) and runs the epilogue; a second
+// round of arrivals lets the last CTA reset the counter. Every mbarrier
+// wait is bounded: one that runs out sets bit 0 of *err and the CTA skips
+// to its teardown (TMEM is always freed).
+#include <algorithm>
+#include <map>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tc_common.cuh"
+
+namespace nmx {
+
+namespace {
+
+using tc::kRecG;
+using tc::mbar_arrive;
+using tc::mbar_expect_tx;
+using tc::mbar_init;
+using tc::mbar_wait;
+using tc::sa_;
+using tc::smem_desc;
+
+constexpr int kDG = 4;                      // dequant warpgroups (they take units in turn)
+constexpr int kSDW = 4 * kDG;               // dequant / epilogue warps
+constexpr int kSThreads = (kSDW + 3) * 32;  // + MMA, x-tile and record-loader warps
+constexpr int kSWMma = kSDW, kSWTma = kSDW + 1, kSWRec = kSDW + 2;
+constexpr int kAST = 4;                     // dequantized weight stages, in TMEM
+constexpr int kAStageCols = 64;             // 128 k of f16, two per 32-bit column
+constexpr int kAccCols = 512 - kAST * kAStageCols;  // accumulator columns
+constexpr int kXSMax = 8;                   // x stages
+constexpr int kRSMax = 16;                  // raw record slots
+using tc::kRecPad;                          // shared-memory stride of a record
+constexpr int kRawSlot = 8 * kRecPad;       // the 8 records of one tile and K block
+constexpr int kMaxTG = 16;                  // weight tiles per CTA
+constexpr int kMaxNT = 128;
+constexpr unsigned kShareSpin = 1u << 22;  // polls of the group counter before giving up
+constexpr size_t kSmemCap = 225 * 1024;  // dynamic shared memory the kernel may ask for (plus 1 KB static)
+
+struct TcsArgs {
+  const unsigned char* w;  // decode records of the whole matrix
+  int M, NT, K, nb;        // rows of x, MMA N, K, K / 128
+  int n_atiles;            // weight tiles (SiLU: 2 per output tile)
+  int tg, S;               // tiles per group, K shares
+  int rs, xs;              // raw slots, x stages
+  uint32_t idesc;
+  long long pair_tiles;    // SiLU: 16-row tile offset of the up rows
+  const half* bias;
+  half* y;
+  long ldy;
+  const half* res;
+  long ldres;
+  float* partials;         // [groups][S][tg][NT][128]
+  unsigned* counters;      // [groups], zero between launches
+  unsigned* err;
+  bool weights_static;
+};
+
+// 16-row record tile r8 (0..7) of weight tile `at`
+template <int EPI>
+__device__ __forceinline__ long long tile16(const TcsArgs& a, int at, int r8) {
+  if constexpr (EPI == EPI_SILU) {
+    const long long o = at >> 1;
+    return (at & 1) ? a.pair_tiles + o * 8 + r8 : o * 8 + r8;
+  } else {
+    return (long long)at * 8 + r8;
+  }
+}
+
+// one output value from the f32 accumulator(s), the GEMM epilogues' rounding
+template <int EPI>
+__device__ __forceinline__ half epi_value(const TcsArgs& a, float acc, float up, int m, long n) {
+  if constexpr (EPI == EPI_SILU) {
+    const float g16 = rnd<half>(acc), u16 = rnd<half>(up);
+    return __float2half_rn(rnd<half>(g16 / (1.0f + expf(-g16))) * u16);
+  } else {
+    float v = rnd<half>(acc);
+    if (a.bias) v = rnd<half>(v + __half2float(a.bias[n]));
+    if constexpr (EPI == EPI_RESID) v += __half2float(a.res[(long)m * a.ldres + n]);
+    return __float2half_rn(v);
+  }
+}
+
+__device__ __forceinline__ void dq_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kSDW * 32) : "memory"); }
+
+// Weight row (record r8 of the tile, row g16 of the record) held by TMEM
+// lane L. The eight lanes of each quarter warp take rows g, g+1 (g even) of
+// four consecutive records, so with records kRecPad apart their 16-byte
+// loads of a row fall in eight different bank groups.
+__device__ __forceinline__ void lane_row(int L, int& r8, int& g16) {
+  const int Q = L >> 3, j = L & 7;
+  r8 = 4 * (Q & 1) + (j & 3);
+  g16 = 8 * ((Q >> 1) & 1) + 2 * (Q >> 2) + (j >> 2);
+}
+
+// D[tmem] (+)= A[tmem] · B[smem]ᵀ, kind::f16
+__device__ __forceinline__ void mma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p; }" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 consecutive 32-bit columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// the 16 words of one record row (both groups) as 128 f16 weights
+// w = s·q + b, two per 32-bit column in k order: group gi in out[gi]
+__device__ __forceinline__ void dequant_row_words(const uint4* c, __half2 s2[2], __half2 s16[2], __half2 b2[2],
+                                                  uint32_t out[2][32]) {
+  const __half2 k1024 = __float2half2_rn(1024.f);
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+#pragma unroll
+    for (int gi = 0; gi < 2; ++gi) {
+#pragma unroll
+      for (int ws = 0; ws < 2; ++ws) {
+        const uint32_t word = gi ? (ws ? c[t].w : c[t].z) : (ws ? c[t].y : c[t].x);
+        const int w = 2 * t + ws;  // word of the group: k 8w .. 8w+7
+        uint32_t P[4];
+        dequant_word<4>(word, P);  // (q0,q4), (16q1,16q5), (q2,q6), (16q3,16q7), each + 1024
+        __half2 v0 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&P[0]), k1024), s2[gi], b2[gi]);
+        __half2 v1 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&P[1]), k1024), s16[gi], b2[gi]);
+        __half2 v2 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&P[2]), k1024), s2[gi], b2[gi]);
+        __half2 v3 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&P[3]), k1024), s16[gi], b2[gi]);
+        const uint32_t u0 = *reinterpret_cast<uint32_t*>(&v0), u1 = *reinterpret_cast<uint32_t*>(&v1);
+        const uint32_t u2 = *reinterpret_cast<uint32_t*>(&v2), u3 = *reinterpret_cast<uint32_t*>(&v3);
+        out[gi][4 * w + 0] = __byte_perm(u0, u1, 0x5410);  // w0, w1
+        out[gi][4 * w + 1] = __byte_perm(u2, u3, 0x5410);  // w2, w3
+        out[gi][4 * w + 2] = __byte_perm(u0, u1, 0x7632);  // w4, w5
+        out[gi][4 * w + 3] = __byte_perm(u2, u3, 0x7632);  // w6, w7
+      }
+    }
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                                                  const __grid_constant__ CUtensorMap tmap_w,
+                                                                  TcsArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // 1024-byte aligned, derived from the shared array itself so that its
+  // loads and stores compile to shared-memory (not generic) accesses
+  unsigned char* smem = smem_raw + ((1024u - (tc::sa_(smem_raw) & 1023u)) & 1023u);
+  __shared__ __align__(8) uint64_t a_full[kAST];
+  __shared__ __align__(8) uint64_t a_empty[kAST];
+  __shared__ __align__(8) uint64_t x_full[kXSMax];
+  __shared__ __align__(8) uint64_t x_empty[kXSMax];
+  __shared__ __align__(8) uint64_t raw_full[kRSMax];
+  __shared__ __align__(8) uint64_t raw_empty[kRSMax];
+  __shared__ __align__(8) uint64_t acc_bar;
+  __shared__ uint32_t s_taddr;
+  __shared__ int s_fail;
+  __shared__ unsigned s_last;  // every share of the group has stored its partials
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int grp = blockIdx.x, share = blockIdx.y;
+  const int t0 = grp * a.tg;
+  const int ntl = min(a.tg, a.n_atiles - t0);  // weight tiles of this CTA
+  const int b0 = int((long long)share * a.nb / a.S), b1 = int((long long)(share + 1) * a.nb / a.S);
+  const int nblk = b1 - b0;
+  const int units = nblk * ntl;  // (block, tile) pairs, block-major
+  const int NT = a.NT;
+  const int xhalf = NT * 128;    // bytes of one 64-k half of an x stage
+  unsigned char* stX = smem;
+  unsigned char* raw = stX + a.xs * 2 * xhalf;
+
+  if (tid == 0) {
+    for (int s = 0; s < kAST; ++s) {
+      mbar_init(&a_full[s], 128);  // one dequant warpgroup per unit
+      mbar_init(&a_empty[s], 1);
+    }
+    for (int s = 0; s < kXSMax; ++s) {
+      mbar_init(&x_full[s], 1);
+      mbar_init(&x_empty[s], 1);
+    }
+    for (int s = 0; s < kRSMax; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], 128);
+    }
+    mbar_init(&acc_bar, 1);
+    s_fail = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kSWMma) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(sa_(&s_taddr))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t taddr = s_taddr;
+
+  if (warp == kSWRec) {
+    // ------------------------------------------------ raw records (weights)
+    if (!a.weights_static) grid_wait();
+    if (lane == 0) {
+      for (int i = 0; i < units; ++i) {
+        const int rs = i % a.rs;
+        if (i >= a.rs && !mbar_wait(&raw_empty[rs], ((i / a.rs) - 1) & 1)) {
+          atomicOr(a.err, 1u);
+          s_fail = 1;
+          break;
+        }
+        const int b = b0 + i / ntl, at = t0 + i % ntl;
+        mbar_expect_tx(&raw_full[rs], kRawSlot);
+        tc::load_records(raw + rs * kRawSlot, &tmap_w, b, int(tile16<EPI>(a, at, 0)), &raw_full[rs]);
+      }
+    }
+  } else if (warp == kSWTma) {
+    // ------------------------------------------------------- x tiles (TMA)
+    grid_wait();
+    if (lane == 0) {
+      for (int bi = 0; bi < nblk; ++bi) {
+        const int xs = bi % a.xs;
+        if (bi >= a.xs && !mbar_wait(&x_empty[xs], ((bi / a.xs) - 1) & 1)) {
+          atomicOr(a.err, 1u);
+          s_fail = 1;
+          break;
+        }
+        unsigned char* dst = stX + xs * 2 * xhalf;
+        mbar_expect_tx(&x_full[xs], 2 * xhalf);
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          asm volatile(
+              "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+              "[%4];" ::"r"(sa_(dst + h * xhalf)),
+              "l"(&tmap_x), "r"((b0 + bi) * 128 + h * 64), "r"(0), "r"(sa_(&x_full[xs]))
+              : "memory");
+      }
+    }
+  } else if (warp == kSWMma) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0) {
+      // one thread issues every MMA: keep its per-MMA work to a few adds
+      // (descriptor start addresses advance in 16-byte units)
+      const uint64_t xdesc0 = smem_desc(stX);
+      const uint32_t xstage_d = uint32_t(2 * xhalf) >> 4, xhalf_d = uint32_t(xhalf) >> 4;
+      const uint32_t a0 = taddr + uint32_t(kAccCols), idesc = a.idesc;
+      bool ok = true;
+      for (int i = 0; i < units && ok; ++i) {
+        const int bi = i / ntl, ti = i - bi * ntl, as = i % kAST, xs = bi % a.xs;
+        if (ti == 0 && !mbar_wait(&x_full[xs], (bi / a.xs) & 1)) ok = false;
+        if (ok && !mbar_wait(&a_full[as], (i / kAST) & 1)) ok = false;
+        if (!ok) {
+          atomicOr(a.err, 1u);
+          s_fail = 1;
+          break;
+        }
+        tc::tc_fence_after();
+        const uint64_t bd = xdesc0 + uint64_t(xs * xstage_d);
+        const uint32_t d = taddr + uint32_t(ti * NT);
+        const uint32_t A = a0 + uint32_t(as * kAStageCols);
+        const uint32_t first = bi ? 1u : 0u;
+#pragma unroll
+        for (int k16 = 0; k16 < 8; ++k16)
+          mma_f16_ta(d, A + 8 * k16, bd + uint64_t((k16 >> 2) * xhalf_d + 2 * (k16 & 3)), idesc,
+                     k16 ? 1u : first);
+        tc::mma_commit(&a_empty[as]);
+        if (ti == ntl - 1) tc::mma_commit(&x_empty[xs]);
+      }
+      tc::mma_commit(&acc_bar);
+    }
+  } else {
+    // ------------------------------------------------ dequantize the tiles
+    // warpgroup dg takes units dg, dg + kDG, ...; thread: TMEM lane L (the
+    // warp's lane quarter), both groups of weight row lane_row(L)
+    const int dg = warp >> 2, L = 32 * (warp & 3) + lane;
+    int r8, g16;
+    lane_row(L, r8, g16);
+    const int rowoff = r8 * kRecPad + (g16 >> 3) * 512 + 64 * (g16 & 7);
+    const int sboff = r8 * kRecPad + 1024 + (g16 & 7) * 4 + (g16 >> 3) * 2;
+    const uint32_t lane_base = taddr + (uint32_t(32 * (warp & 3)) << 16);
+    for (int i = dg; i < units; i += kDG) {
+      const int as = i % kAST, rs = i % a.rs;
+      if (i >= kAST && !mbar_wait(&a_empty[as], ((i / kAST) - 1) & 1)) {
+        atomicOr(a.err, 1u);
+        s_fail = 1;
+        break;
+      }
+      if (!mbar_wait(&raw_full[rs], (i / a.rs) & 1)) {
+        atomicOr(a.err, 1u);
+        s_fail = 1;
+        break;
+      }
+      const unsigned char* slot = raw + rs * kRawSlot;
+      uint4 c[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) c[t] = *reinterpret_cast<const uint4*>(slot + rowoff + 16 * t);
+      __half2 s2[2], s16[2], b2[2];
+#pragma unroll
+      for (int gi = 0; gi < 2; ++gi) {
+        const __half sc = *reinterpret_cast<const __half*>(slot + sboff + gi * 32);
+        const __half bi = *reinterpret_cast<const __half*>(slot + sboff + 64 + gi * 32);
+        s2[gi] = __halves2half2(sc, sc);
+        s16[gi] = __hmul2(s2[gi], __float2half2_rn(0.0625f));
+        b2[gi] = __halves2half2(bi, bi);
+      }
+      uint32_t out[2][32];
+      dequant_row_words(c, s2, s16, b2, out);
+      mbar_arrive(&raw_empty[rs]);  // the slot's bytes are in registers
+      tc::tc_fence_after();         // after the wait for the stage's last MMAs
+      const uint32_t acol = lane_base + uint32_t(kAccCols + as * kAStageCols);
+      tmem_st32(acol, out[0]);
+      tmem_st32(acol + 32, out[1]);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc::tc_fence_before();
+      mbar_arrive(&a_full[as]);
+    }
+
+    // ------------------------------------------------------------ epilogue
+    if (!mbar_wait(&acc_bar, 0)) {
+      atomicOr(a.err, 1u);
+      s_fail = 1;
+    }
+    tc::tc_fence_after();
+    grid_wait();  // y, the residual and the partial scratch follow the previous kernel
+    const int quad = warp & 3, part = warp >> 2;  // lane quarter; 8-column chunks part, part + kDG, ...
+    const int tlane = 32 * quad + lane;  // this thread's TMEM lane
+    int er8, eg16;
+    lane_row(tlane, er8, eg16);
+    const int trow = er8 * 16 + eg16;    // and the weight row of the tile it holds
+    const uint32_t lane_addr = taddr + (uint32_t(32 * quad) << 16);
+    const bool ok = !s_fail;
+    if (a.S == 1) {
+      constexpr int STEP = EPI == EPI_SILU ? 2 : 1;
+      for (int ti = 0; ti < ntl; ti += STEP) {
+        const long n = EPI == EPI_SILU ? (long)((t0 + ti) >> 1) * 128 + trow : (long)(t0 + ti) * 128 + trow;
+        for (int c0 = 8 * part; c0 < NT; c0 += 8 * kDG) {
+          float v[8], u[8];
+          tc::tmem_ld8(lane_addr + uint32_t(ti * NT + c0), v);
+          if constexpr (EPI == EPI_SILU) tc::tmem_ld8(lane_addr + uint32_t((ti + 1) * NT + c0), u);
+          if (ok) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int m = c0 + j;
+              if (m < a.M) a.y[(long)m * a.ldy + n] = epi_value<EPI>(a, v[j], EPI == EPI_SILU ? u[j] : 0.f, m, n);
+            }
+          }
+        }
+      }
+    } else {
+      // partial tiles of this share: [tile][m][row], row fastest
+      float* P = a.partials + ((size_t)grp * a.S + share) * a.tg * NT * 128;
+      for (int ti = 0; ti < ntl; ++ti) {
+        for (int c0 = 8 * part; c0 < NT; c0 += 8 * kDG) {
+          float v[8];
+          tc::tmem_ld8(lane_addr + uint32_t(ti * NT + c0), v);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (c0 + j < a.M) __stcg(P + ((size_t)ti * NT + c0 + j) * 128 + tlane, v[j]);
+        }
+      }
+      __threadfence();
+      dq_bar();
+      if (tid == 0) {
+        // every share's partials are in place (the grid is one wave, so the
+        // other shares are resident or done; the wait is bounded)
+        unsigned* ctr = a.counters + grp;
+        atomicAdd(ctr, 1u);
+        unsigned v = 0;
+        for (unsigned it = 0; it < kShareSpin; ++it) {
+          asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+          if (v >= unsigned(a.S)) break;
+          __nanosleep(64);
+        }
+        s_last = v >= unsigned(a.S) ? 1u : 0u;
+        if (!s_last) atomicOr(a.err, 1u);
+      }
+      dq_bar();
+      // this share's slice of the group's outputs, 4 rows per item, partials
+      // summed in share order
+      const bool all_in = s_last != 0u;
+      const size_t share_stride = (size_t)a.tg * NT * 128;
+      const float* Pg = a.partials + (size_t)grp * a.S * share_stride;
+      constexpr int STEP = EPI == EPI_SILU ? 2 : 1;
+      const int E4 = (ntl / STEP) * a.M * 32;
+      const int e_lo = int((long long)share * E4 / a.S), e_hi = int((long long)(share + 1) * E4 / a.S);
+      for (int e = e_lo + tid; e < e_hi; e += kSDW * 32) {
+        const int r4 = e & 31, m = (e >> 5) % a.M, ti = ((e >> 5) / a.M) * STEP;
+        const float* base = Pg + ((size_t)ti * NT + m) * 128 + 4 * r4;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f), up = acc;
+#pragma unroll 4
+        for (int sh = 0; sh < a.S; ++sh) {
+          const float4 v = __ldcg(reinterpret_cast<const float4*>(base + sh * share_stride));
+          acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+          if constexpr (EPI == EPI_SILU) {
+            const float4 u = __ldcg(reinterpret_cast<const float4*>(base + NT * 128 + sh * share_stride));
+            up.x += u.x; up.y += u.y; up.z += u.z; up.w += u.w;
+          }
+        }
+        const long n0 = (EPI == EPI_SILU ? (long)((t0 + ti) >> 1) : (long)(t0 + ti)) * 128;
+        if (ok && all_in) {
+          const float av[4] = {acc.x, acc.y, acc.z, acc.w}, uv[4] = {up.x, up.y, up.z, up.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            int pr8, pg16;
+            lane_row(4 * r4 + q, pr8, pg16);
+            const long n = n0 + pr8 * 16 + pg16;
+            a.y[(long)m * a.ldy + n] = epi_value<EPI>(a, av[q], uv[q], m, n);
+          }
+        }
+      }
+      // the second round of arrivals: the last share resets the counter
+      dq_bar();
+      if (tid == 0 && atomicAdd(a.counters + grp, 1u) == unsigned(2 * a.S - 1)) a.counters[grp] = 0u;
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  grid_launch_dependents();
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == kSWMma) {
+    tc::tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(taddr) : "memory");
+  }
+}
+
+struct TcsPlan {
+  int NT = 0, tg = 0, groups = 0, S = 0, rs = 0, xs = 0;
+  size_t smem = 0, partial_floats = 0;
+};
+
+// Tiles per group and K shares: the fewest weight units (tile × K block) on
+// the busiest CTA over one wave of SMs, with the x tile's L2 reads and the
+// partial sums' round trip counted against it.
+TcsPlan plan_tcs(int M, int N_out, int K, int epi, int num_sms) {
+  TcsPlan p;
+  p.NT = (M + 15) / 16 * 16;
+  const int apt = epi == EPI_SILU ? 2 : 1;
+  const int n_ot = N_out / 128, nb = K / 128;
+  const int tg_max = std::min(kMaxTG, kAccCols / p.NT) / apt * apt;
+  double best = 1e30;
+  for (int tgo = 1; tgo * apt <= tg_max; ++tgo) {
+    const int tga = tgo * apt;
+    const int groups = (n_ot + tgo - 1) / tgo;
+    for (int S = 1; S <= nb; ++S) {
+      const long long ctas = (long long)groups * S;
+      const long long waves = (ctas + num_sms - 1) / num_sms;
+      if (waves > 1 && S > 1) break;
+      const int upc = tga * ((nb + S - 1) / S);
+      const double x_cost = 0.5 * double(p.NT) * 256.0 / (double(tga) * 8 * kRecG);
+      const double p_cost = S > 1 ? 0.5 * double(tga) * p.NT * 128 * 8 / (double(upc) * 8 * kRecG) : 0.0;
+      const double cost = double(waves) * upc * (1.0 + x_cost + p_cost) + 1e-6 * double(ctas);
+      if (cost < best) {
+        best = cost;
+        p.tg = tga;
+        p.groups = groups;
+        p.S = S;
+      }
+    }
+  }
+  // x stages to cover the L2 latency of the x tiles (shared by tg units),
+  // the rest of shared memory for raw record slots
+  const size_t xstage = size_t(2) * p.NT * 128;
+  p.xs = std::max(2, std::min(kXSMax, int((kSmemCap - 1024 - 6 * size_t(kRawSlot)) / xstage)));
+  p.xs = std::min(p.xs, std::max(2, 8 / std::max(1, p.tg / (epi == EPI_SILU ? 2 : 1))));
+  const size_t fixed = size_t(p.xs) * xstage + 1024;
+  p.rs = int(std::min<size_t>(kRSMax, (kSmemCap - fixed) / kRawSlot));
+  p.smem = fixed + size_t(p.rs) * kRawSlot;
+  p.partial_floats = p.S > 1 ? size_t(p.groups) * p.S * p.tg * p.NT * 128 : 0;
+  return p;
+}
+
+template <int EPI>
+nmx_status_t launch_tcs(Ctx* c, const CUtensorMap& tm, const CUtensorMap& tw, const TcsArgs& g, const TcsPlan& p) {
+  static std::mutex mu;
+  static std::map<int, bool> set;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!set[c->device]) {
+      NMX_CUDA_OK(cudaFuncSetAttribute(qgemm_tcs_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(kSmemCap)));
+      set[c->device] = true;
+    }
+  }
+  return launch(c, qgemm_tcs_kernel<EPI>, dim3(p.groups, p.S), dim3(kSThreads), p.smem, tm, tw, g);
+}
+
+}  // namespace
+
+bool qgemm_tcs_supported(int M, int N_out, int K, int epi) {
+  if (M < 1 || M > kMaxNT || K <= 0 || K % 128 != 0 || N_out % 128 != 0) return false;
+  return epi == EPI_STORE || epi == EPI_RESID || epi == EPI_SILU;
+}
+
+size_t qgemm_tcs_partials_floats(int M, int N_out, int K, int epi, int num_sms) {
+  if (!qgemm_tcs_supported(M, N_out, K, epi)) return 0;
+  return plan_tcs(M, N_out, K, epi, num_sms).partial_floats;
+}
+
+int qgemm_tcs_groups(int M, int N_out, int K, int epi, int num_sms) {
+  if (!qgemm_tcs_supported(M, N_out, K, epi)) return 0;
+  return plan_tcs(M, N_out, K, epi, num_sms).groups;
+}
+
+nmx_status_t qgemm_tcs(Ctx* c, const GemvDLArgs& a, int epi) {
+  NMX_CHECK(qgemm_tcs_supported(a.M, a.N, a.K, epi), NMX_ERR_UNSUPPORTED, "qgemm_tcs: shape or epilogue");
+  NMX_CHECK(a.gamma == nullptr, NMX_ERR_UNSUPPORTED, "qgemm_tcs: normalise x first");
+  NMX_CHECK(a.err != nullptr, NMX_ERR_INVALID, "qgemm_tcs: no error word");
+  NMX_CHECK(reinterpret_cast<uintptr_t>(a.x) % 16 == 0 && (a.ldx * 2) % 16 == 0, NMX_ERR_UNSUPPORTED,
+            "qgemm_tcs: x must be 16-byte aligned with a 16-byte row pitch");
+  NMX_CHECK(reinterpret_cast<uintptr_t>(a.w) % 16 == 0, NMX_ERR_INVALID, "qgemm_tcs: records must be 16-byte aligned");
+  const TcsPlan p = plan_tcs(a.M, a.N, a.K, epi, c->num_sms);
+  if (p.S > 1) {
+    NMX_CHECK(a.partials != nullptr && a.partials_cap >= p.partial_floats && a.counters != nullptr,
+              NMX_ERR_INVALID, "qgemm_tcs: partial-sum scratch too small");
+  }
+  CUtensorMap tm, tw;
+  NMX_TRY(tc::encode_x_map(&tm, a.x, a.ldx, a.M, a.K, p.NT));
+  const long long rows = epi == EPI_SILU ? (long long)a.pair_tiles * 16 + a.N : a.N;
+  NMX_TRY(tc::encode_records_map(&tw, a.w, a.K / 128, rows / 16, 8));
+  TcsArgs g;
+  g.w = static_cast<const unsigned char*>(a.w);
+  g.M = a.M;
+  g.NT = p.NT;
+  g.K = a.K;
+  g.nb = a.K / 128;
+  g.n_atiles = (a.N / 128) * (epi == EPI_SILU ? 2 : 1);
+  g.tg = p.tg;
+  g.S = p.S;
+  g.rs = p.rs;
+  g.xs = p.xs;
+  g.idesc = tc::idesc_f16(128, p.NT);
+  g.pair_tiles = a.pair_tiles;
+  g.bias = static_cast<const half*>(a.bias);
+  g.y = static_cast<half*>(a.y);
+  g.ldy = a.ldy;
+  g.res = static_cast<const half*>(a.res);
+  g.ldres = a.ldres;
+  g.partials = a.partials;
+  g.counters = a.counters;
+  g.err = a.err;
+  g.weights_static = a.weights_static;
+  switch (epi) {
+    case EPI_STORE: return launch_tcs<EPI_STORE>(c, tm, tw, g, p);
+    case EPI_RESID: return launch_tcs<EPI_RESID>(c, tm, tw, g, p);
+    default: return launch_tcs<EPI_SILU>(c, tm, tw, g, p);
+  }
+}
+
+}  // namespace nmx

@@ -87,6 +87,16 @@ nmx_status_t qgemv_dl(Ctx* c, const GemvDLArgs& a, int epi);
 bool qgemm_tc_supported(int N_out, int K, int epi);
 nmx_status_t qgemm_tc(Ctx* c, const GemvDLArgs& a, int epi);
 constexpr int kGemmMinRows = 64;  // qgemv_dl hands row counts from here on to qgemm_tc
+// tensor-core GEMM for decode batches (weights as the MMA's 128 rows,
+// activation rows as its N, K split over the SMs): 1..128 rows, N_out % 128,
+// K % 128; store / residual / SiLU·up epilogues, no RMSNorm prologue
+constexpr int kTcsMinRows = 9;    // qgemv_dl hands kTcsMinRows..kTcsMaxRows rows to qgemm_tcs
+constexpr int kTcsMaxRows = 128;
+bool qgemm_tcs_supported(int M, int N_out, int K, int epi);
+// floats of partial-sum scratch (partials) and counters one launch needs
+size_t qgemm_tcs_partials_floats(int M, int N_out, int K, int epi, int num_sms);
+int qgemm_tcs_groups(int M, int N_out, int K, int epi, int num_sms);
+nmx_status_t qgemm_tcs(Ctx* c, const GemvDLArgs& a, int epi);
 // 1..8 activation rows (qgemv_dl dispatches here when the staging fits)
 bool qgemv_small_fits(int M, int N_out, int K, int epi, int num_sms);
 size_t qgemv_small_partials_floats(int N_out, int K, int epi, int num_sms);

@@ -205,8 +205,12 @@ nmx_status_t Model::create(Ctx* c, const nmx_model_cfg& cfg, Model** out) {
     auto need = [&](const Lin& l, bool paired) {
       if (!l.dl) return;
       const int n_out = paired ? l.N / 2 : l.N;
-      pf = std::max(pf, qgemv_dl_partials_floats(n_out, l.K, paired ? EPI_SILU : EPI_STORE, c->num_sms,
-                                                 m->dl_ctas_per_sm));
+      const int epi = paired ? EPI_SILU : EPI_STORE;
+      pf = std::max(pf, qgemv_dl_partials_floats(n_out, l.K, epi, c->num_sms, m->dl_ctas_per_sm));
+      // decode batches and short prefill chunks on the tensor-core decode GEMM
+      const int rows_max = std::min(kTcsMaxRows, std::max(m->max_batch, m->max_tokens));
+      for (int rows = 16; rows < rows_max + 16; rows += 16)
+        pf = std::max(pf, qgemm_tcs_partials_floats(std::min(rows, rows_max), n_out, l.K, epi, c->num_sms));
       ntg = std::max(ntg, size_t(n_out / 16));
     };
     need(m->lm, false);
@@ -508,9 +512,11 @@ KvPool::~KvPool() {
 nmx_status_t Model::linear(const Lin& l, const void* x, long ldx, const void* gamma, int M, int N_out,
                            long pair_off_rows, const void* bias, void* y, long ldy, const void* res, long ldres,
                            int epi, float* logits_f32, int* ids, int* next_tokens) {
-  if (l.dl && M >= kGemmMinRows && qgemm_tc_supported(N_out, l.K, epi)) {
-    // many rows (prefill): the tensor-core GEMM, after the RMSNorm it has no
-    // prologue for
+  const bool tc_prefill = l.dl && M > kTcsMaxRows && qgemm_tc_supported(N_out, l.K, epi);
+  const bool tc_batch = l.dl && !tc_prefill && M >= kTcsMinRows && qgemm_tcs_supported(M, N_out, l.K, epi);
+  if (tc_prefill || tc_batch || (l.dl && M >= kGemmMinRows && qgemm_tc_supported(N_out, l.K, epi))) {
+    // decode batches and prefill: the tensor-core GEMMs, after the RMSNorm
+    // they have no prologue for
     if (gamma) {
       NMX_TRY(rmsnorm(ctx, x, ldx, gamma, M, l.K, cfg.rms_eps, NMX_F16, xn, l.K));
       x = xn;
@@ -520,6 +526,11 @@ nmx_status_t Model::linear(const Lin& l, const void* x, long ldx, const void* ga
     a.x = x; a.ldx = ldx; a.w = l.w; a.N = N_out; a.K = l.K; a.M = M; a.pair_tiles = pair_off_rows / 16;
     a.bias = bias; a.y = y; a.ldy = ldy; a.res = res; a.ldres = ldres;
     a.err = ctx->dev_err;
+    a.weights_static = true;
+    if (tc_batch) {
+      a.partials = dl_partials; a.partials_cap = dl_partials_cap; a.counters = dl_counters;
+      return qgemm_tcs(ctx, a, epi);
+    }
     return qgemm_tc(ctx, a, epi);
   }
   if (l.dl) {

@@ -511,9 +511,15 @@ int qgemv_dl_max_m(int K, int epi) {
 nmx_status_t qgemv_dl(Ctx* c, const GemvDLArgs& a, int epi) {
   NMX_CHECK(a.M > 0 && a.N % 16 == 0 && a.K % 128 == 0 && (long long)(a.N / 16) * (a.K / 128) >= kWarps,
             NMX_ERR_UNSUPPORTED, "qgemv_dl: bad shape");
-  // many rows: the tensor-core GEMM
-  if (a.M >= kGemmMinRows && a.gamma == nullptr && a.err != nullptr && qgemm_tc_supported(a.N, a.K, epi))
-    return qgemm_tc(c, a, epi);
+  // tensor-core GEMMs: decode batches (weights as the MMA rows, K split over
+  // the SMs), and prefill row counts
+  if (a.gamma == nullptr && a.err != nullptr) {
+    if (a.M > kTcsMaxRows && qgemm_tc_supported(a.N, a.K, epi)) return qgemm_tc(c, a, epi);
+    if (a.M >= kTcsMinRows && qgemm_tcs_supported(a.M, a.N, a.K, epi) && a.counters &&
+        qgemm_tcs_partials_floats(a.M, a.N, a.K, epi, c->num_sms) <= (a.partials ? a.partials_cap : 0))
+      return qgemm_tcs(c, a, epi);
+    if (a.M >= kGemmMinRows && qgemm_tc_supported(a.N, a.K, epi)) return qgemm_tc(c, a, epi);
+  }
   // up to eight rows: the small-batch kernel, in as few launches as its
   // staging allows
   if (a.M <= 8) {

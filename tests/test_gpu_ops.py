@@ -146,6 +146,31 @@ def test_qmatmul_records_tensor_core_gemm(env, M, N, K):
     assert O.cosine(got.ravel(), ref.ravel()) > 0.99999
 
 
+@pytest.mark.parametrize("M,N,K", [(9, 4096, 4096), (16, 1024, 512), (33, 6144, 1024), (64, 4096, 4096),
+                                   (80, 16384, 1024), (128, 1024, 2048), (100, 512, 14336)])
+def test_qmatmul_records_decode_batch_gemm(env, M, N, K):
+    """9..128 rows go through the decode-batch tcgen05 GEMM (weights as the
+    MMA's rows, rows of x as its columns, K split over the SMs with a
+    deterministic last-arriver sum): equals the oracle in one launch, and
+    repeated calls agree bit for bit."""
+    torch, nmx, ctx = env
+    rng = np.random.default_rng(7 * M + N + K)
+    w = rng.standard_normal((N, K), dtype=np.float32) * 0.02
+    wq, s, b = O.quantize(w, 4, 64)
+    x = O.f32_to_f16bits(rng.standard_normal((M, K), dtype=np.float32))
+    ref = O.f16bits_to_f32(O.qmatmul(x, wq, s, b, 4, 64))
+    rec = ctx.pack_records(dev(torch, wq.view(np.int32)), u16(torch, s), u16(torch, b))
+    xd = u16(torch, x)
+    n0 = ctx.launches
+    y = ctx.quantized_matmul_records(xd, rec, N)
+    assert ctx.launches - n0 == 1
+    got = O.f16bits_to_f32(host16(y))
+    assert O.max_rel_err(got, ref) <= 2e-3, (M, N, K)
+    assert O.cosine(got.ravel(), ref.ravel()) > 0.99999
+    again = host16(ctx.quantized_matmul_records(xd, rec, N))
+    assert np.array_equal(again, host16(y))
+
+
 @pytest.mark.parametrize("M,N,K", [(1, 6144, 4096), (1, 4096, 4096), (3, 5120, 1024), (1, 512, 640 // 128 * 128)])
 def test_qmatmul_records_deterministic(env, M, N, K):
     """Split tile groups are summed in a fixed order: repeated calls agree bit for bit."""
