@@ -240,25 +240,34 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
     // ------------------------------------------------ raw records (weights)
     if (!a.weights_static) grid_wait();
     if (lane == 0) {
+      // single-thread loops keep ring positions as counters: a runtime
+      // division per unit would cost more than the unit's issue work
+      int rs = 0, rph = 0, b = b0, ti = 0;
       for (int i = 0; i < units; ++i) {
-        const int rs = i % a.rs;
-        if (i >= a.rs && !mbar_wait(&raw_empty[rs], ((i / a.rs) - 1) & 1)) {
+        if (i >= a.rs && !mbar_wait(&raw_empty[rs], rph ^ 1)) {
           atomicOr(a.err, 1u);
           s_fail = 1;
           break;
         }
-        const int b = b0 + i / ntl, at = t0 + i % ntl;
         mbar_expect_tx(&raw_full[rs], kRawSlot);
-        tc::load_records(raw + rs * kRawSlot, &tmap_w, b, int(tile16<EPI>(a, at, 0)), &raw_full[rs]);
+        tc::load_records(raw + rs * kRawSlot, &tmap_w, b, int(tile16<EPI>(a, t0 + ti, 0)), &raw_full[rs]);
+        if (++rs == a.rs) {
+          rs = 0;
+          rph ^= 1;
+        }
+        if (++ti == ntl) {
+          ti = 0;
+          ++b;
+        }
       }
     }
   } else if (warp == kSWTma) {
     // ------------------------------------------------------- x tiles (TMA)
     grid_wait();
     if (lane == 0) {
+      int xs = 0, xph = 0;
       for (int bi = 0; bi < nblk; ++bi) {
-        const int xs = bi % a.xs;
-        if (bi >= a.xs && !mbar_wait(&x_empty[xs], ((bi / a.xs) - 1) & 1)) {
+        if (bi >= a.xs && !mbar_wait(&x_empty[xs], xph ^ 1)) {
           atomicOr(a.err, 1u);
           s_fail = 1;
           break;
@@ -272,6 +281,10 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
               "[%4];" ::"r"(sa_(dst + h * xhalf)),
               "l"(&tmap_x), "r"((b0 + bi) * 128 + h * 64), "r"(0), "r"(sa_(&x_full[xs]))
               : "memory");
+        if (++xs == a.xs) {
+          xs = 0;
+          xph ^= 1;
+        }
       }
     }
   } else if (warp == kSWMma) {
@@ -282,11 +295,11 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
       const uint64_t xdesc0 = smem_desc(stX);
       const uint32_t xstage_d = uint32_t(2 * xhalf) >> 4, xhalf_d = uint32_t(xhalf) >> 4;
       const uint32_t a0 = taddr + uint32_t(kAccCols), idesc = a.idesc;
-      bool ok = true;
-      for (int i = 0; i < units && ok; ++i) {
-        const int bi = i / ntl, ti = i - bi * ntl, as = i % kAST, xs = bi % a.xs;
-        if (ti == 0 && !mbar_wait(&x_full[xs], (bi / a.xs) & 1)) ok = false;
-        if (ok && !mbar_wait(&a_full[as], (i / kAST) & 1)) ok = false;
+      int ti = 0, as = 0, aph = 0, xs = 0, xph = 0;
+      uint32_t first = 0u;  // 0 until the first block is in the accumulators
+      for (int i = 0; i < units; ++i) {
+        bool ok = !(ti == 0 && !mbar_wait(&x_full[xs], xph));
+        if (ok && !mbar_wait(&a_full[as], aph)) ok = false;
         if (!ok) {
           atomicOr(a.err, 1u);
           s_fail = 1;
@@ -296,13 +309,24 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
         const uint64_t bd = xdesc0 + uint64_t(xs * xstage_d);
         const uint32_t d = taddr + uint32_t(ti * NT);
         const uint32_t A = a0 + uint32_t(as * kAStageCols);
-        const uint32_t first = bi ? 1u : 0u;
 #pragma unroll
         for (int k16 = 0; k16 < 8; ++k16)
           mma_f16_ta(d, A + 8 * k16, bd + uint64_t((k16 >> 2) * xhalf_d + 2 * (k16 & 3)), idesc,
                      k16 ? 1u : first);
         tc::mma_commit(&a_empty[as]);
-        if (ti == ntl - 1) tc::mma_commit(&x_empty[xs]);
+        if (++as == kAST) {
+          as = 0;
+          aph ^= 1;
+        }
+        if (++ti == ntl) {
+          tc::mma_commit(&x_empty[xs]);
+          ti = 0;
+          first = 1u;
+          if (++xs == a.xs) {
+            xs = 0;
+            xph ^= 1;
+          }
+        }
       }
       tc::mma_commit(&acc_bar);
     }
@@ -316,14 +340,16 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
     const int rowoff = r8 * kRecPad + (g16 >> 3) * 512 + 64 * (g16 & 7);
     const int sboff = r8 * kRecPad + 1024 + (g16 & 7) * 4 + (g16 >> 3) * 2;
     const uint32_t lane_base = taddr + (uint32_t(32 * (warp & 3)) << 16);
+    static_assert(kDG == kAST, "warpgroup dg owns A stage dg");
+    const int as = dg;
+    int rs = dg % a.rs, rph = (dg / a.rs) & 1;
     for (int i = dg; i < units; i += kDG) {
-      const int as = i % kAST, rs = i % a.rs;
       if (i >= kAST && !mbar_wait(&a_empty[as], ((i / kAST) - 1) & 1)) {
         atomicOr(a.err, 1u);
         s_fail = 1;
         break;
       }
-      if (!mbar_wait(&raw_full[rs], (i / a.rs) & 1)) {
+      if (!mbar_wait(&raw_full[rs], rph)) {
         atomicOr(a.err, 1u);
         s_fail = 1;
         break;
@@ -351,6 +377,11 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc::tc_fence_before();
       mbar_arrive(&a_full[as]);
+      rs += kDG;
+      while (rs >= a.rs) {
+        rs -= a.rs;
+        rph ^= 1;
+      }
     }
 
     // ------------------------------------------------------------ epilogue

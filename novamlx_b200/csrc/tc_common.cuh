@@ -27,20 +27,20 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* b, unsigned bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sa_(b)), "r"(bytes) : "memory");
 }
+__device__ __forceinline__ bool mbar_try(unsigned a, unsigned parity) {
+  unsigned ok;
+  asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+               : "=r"(ok)
+               : "r"(a), "r"(parity)
+               : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity) {
   const unsigned a = sa_(b);
-  for (unsigned it = 0; it < kGSpin; ++it) {
-    unsigned ok;
-    asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-        : "=r"(ok)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (ok) return true;
-  }
+  for (unsigned it = 0; it < kGSpin; ++it)
+    if (mbar_try(a, parity)) return true;
   return false;
 }
-
 // K-major operand in the 128-byte swizzle: 8-row groups 1024 B apart (SBO),
 // version 1, layout SWIZZLE_128B (2); the start address steps 32 B per k16
 __device__ __forceinline__ uint64_t smem_desc(const void* p) {
