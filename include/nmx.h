@@ -449,6 +449,53 @@ NMX_API nmx_status_t nmx_sched_poll(nmx_sched_t sched, int64_t request_id, int32
                                     int max_tokens, int* n_tokens, int* state);
 NMX_API nmx_status_t nmx_sched_stats(nmx_sched_t sched, nmx_sched_stats_t* out);
 
+/* ------------------------------------------------------------------------ */
+/* Speculative decoding. */
+
+/* N-gram draft source (NGramSpeculator, Sources/NovaMLXEngine/CompiledSampler.swift:60-204,
+ * and SpeculativeDecoder's acceptance count, :206-250): continuations of the
+ * last ngram_size tokens, up to max_draft distinct ones per n-gram, offered
+ * once the n-gram has min_hits hits; the cache is cut to max_cache_size / 2
+ * entries (fewest hits first, older first on ties) when it outgrows the cap. */
+typedef struct nmx_ngram_s* nmx_ngram_t;
+NMX_API nmx_status_t nmx_ngram_create(int ngram_size, int max_draft, int min_hits, int max_cache_size,
+                                      nmx_ngram_t* out);
+NMX_API void nmx_ngram_destroy(nmx_ngram_t ngram);
+NMX_API void nmx_ngram_record_token(nmx_ngram_t ngram, int32_t token);
+NMX_API void nmx_ngram_record_tokens(nmx_ngram_t ngram, const int32_t* tokens, int n_tokens);
+/* Drafts for the context's last n-gram (context NULL: the recorded token
+ * buffer); returns how many were written (0 .. min(max_draft, max_drafts)). */
+NMX_API int nmx_ngram_speculate(nmx_ngram_t ngram, const int32_t* context, int n_context, int32_t* out_drafts,
+                                int max_drafts);
+/* recordAccepted: record the tokens and count n_tokens proposed, accepted accepted. */
+NMX_API void nmx_ngram_record_accepted(nmx_ngram_t ngram, const int32_t* tokens, int n_tokens, int accepted);
+NMX_API void nmx_ngram_stats(nmx_ngram_t ngram, int* cache_size, long long* total_hits, int* buffer_size,
+                             double* acceptance_rate);
+
+/* Verification of drafted tokens (FusedBatchScheduler.swift:1247-1300): ONE
+ * forward over [last_token] + drafts of every sequence (its K/V appended at
+ * start_pos ..), the greedy id at every position, then per sequence:
+ *   NMX_VERIFY_NGRAM:  the reference's n-gram rule as written — tokens =
+ *     [g0, g1, ..., g_p] up to and including the first p >= 1 with
+ *     g_p != drafts[p-1]; accepted = the number of matches;
+ *   NMX_VERIFY_PREFIX: draft-model verification — accepted = the longest
+ *     prefix with drafts[i] == g_i; tokens = drafts[0..accepted) + [g_accepted].
+ * out_tokens is [n_seqs][max n_drafts + 1]; out_counts[i] tokens of row i are
+ * valid. The pages past the kept positions are simply overwritten later
+ * (the cache "trim"). */
+typedef enum { NMX_VERIFY_NGRAM = 0, NMX_VERIFY_PREFIX = 1 } nmx_verify_rule_t;
+typedef struct {
+  int32_t last_token;
+  const int32_t* drafts;
+  int n_drafts;
+  int start_pos;                /* position of last_token */
+  const int32_t* block_table;
+  int n_blocks;
+} nmx_spec_seq_t;
+NMX_API nmx_status_t nmx_spec_verify(nmx_model_t model, nmx_kv_pool_t pool, const nmx_spec_seq_t* seqs, int n_seqs,
+                                     nmx_verify_rule_t rule, int32_t* out_tokens, int* out_counts,
+                                     int* out_accepted);
+
 #ifdef __cplusplus
 }
 #endif

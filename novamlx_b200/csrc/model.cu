@@ -621,6 +621,23 @@ nmx_status_t Model::run_layers_prefill(KvPool* pool, int T) {
 nmx_status_t Model::run_head(const void* x, int rows, bool want_logits, int* next_tokens) {
   Ctx* c = ctx;
   const int H = cfg.hidden, V = cfg.vocab;
+  if (!want_logits && lm.dl && rows >= kTcsMinRows && qgemm_tcs_supported(std::min(rows, kTcsMaxRows), V, H, EPI_STORE)) {
+    // many rows (a decode batch, a verify block): f16 logits from the
+    // tensor-core decode GEMM (one pass over the head's weights per 128
+    // rows) into the logits scratch, then a row-wise argmax over them (the
+    // GEMV argmax epilogue's rule: f16-rounded values, lowest id on ties)
+    half* lg = reinterpret_cast<half*>(logits_f32);
+    for (int r0 = 0; r0 < rows; r0 += kTcsMaxRows) {
+      const int rc = std::min(kTcsMaxRows, rows - r0);
+      NMX_TRY(linear(lm, static_cast<const char*>(x) + size_t(r0) * H * 2, H, final_norm, rc, V, 0, nullptr,
+                     lg + size_t(r0) * V, V, nullptr, 0, EPI_STORE));
+      NMX_TRY(argmax_rows(c, lg + size_t(r0) * V, rc, V, NMX_F16, out_ids + r0));
+      if (next_tokens)
+        NMX_CUDA_OK(cudaMemcpyAsync(next_tokens + r0, out_ids + r0, size_t(rc) * 4, cudaMemcpyDeviceToDevice,
+                                    c->stream));
+    }
+    return NMX_OK;
+  }
   const int chunk = lm.dl ? std::min(32, qgemv_dl_max_m(H, EPI_ARGMAX)) : 32;
   for (int r0 = 0; r0 < rows; r0 += chunk) {
     const int rc = std::min(chunk, rows - r0);

@@ -5,6 +5,7 @@
   python -m novamlx_b200.microbench attn [--batch 1] [--ctx 2176]
   python -m novamlx_b200.microbench decode [--layers 2] [--ctx 2048] [--tokens 64] [--batch 1]
   python -m novamlx_b200.microbench serve [--layers 32] [--seqs 64] [--tokens 256]
+  python -m novamlx_b200.microbench spec [--batch 16] [--ctx 4096] [--drafts 4] [--cycles 8] [--oracle-draft]
 
 gemv: the decode-record GEMV (nmx_op_qmatmul_records) over `copies` distinct
 weight copies, so the weights come from HBM on every launch.
@@ -27,6 +28,18 @@ in [2064, 4096]), the others uniform in [512, 4096] tokens; each decodes
 aggregate generated tok/s over the whole run, the tok/s of the steps where
 every running sequence decodes, the prefix-cache hit tokens, and the
 distinct vs logical KV pages at the widest decode step.
+
+spec: speculative decoding with a Llama-3.3-70B-style target and a
+Llama-3.2-1B-style draft (random 4-bit weights, --layers / --draft-layers
+layers): --batch sequences at context --ctx; per cycle the draft decodes
+--drafts greedy ids per sequence (nmx_decode_greedy) and the target verifies
+[last] + drafts in one forward (nmx_spec_verify, prefix rule: M = batch ×
+(drafts + 1) rows). Random weights accept almost nothing, so the acceptance
+is reported as measured; --oracle-draft replaces the drafts by the target's
+own greedy continuation (computed before the timed cycles) for the
+full-acceptance verify throughput. The pages before --ctx are left as
+allocated (zeros): the timed work, reading ctx positions of K/V per row, is
+the same as after a real prefill.
 
 Prints one JSON line per run with the average launch duration measured by
 CUDA events on the library's stream and the algorithmic bytes per launch.
@@ -194,13 +207,84 @@ def serve(ctx, torch, nmx, layers, n_seqs, tokens, step_tokens, chunk, seed=0):
             "kv_bytes_per_token": bpt, "weight_bytes_per_step": m.step_weight_bytes}
 
 
+def spec(ctx, torch, nmx, batch, ctx_len, n_drafts, cycles, layers, draft_layers, oracle_draft):
+    import numpy as np
+    D = n_drafts
+    tcfg = nmx.llama33_70b(n_layers=layers, max_batch=batch, max_tokens=batch * (D + 1))
+    target = nmx.Model(ctx, tcfg)
+    target.init_random(seed=0, std=0.02)
+    dcfg = nmx.llama32_1b(n_layers=draft_layers, max_batch=batch, max_tokens=batch)
+    draft = nmx.Model(ctx, dcfg)
+    draft.init_random(seed=1, std=0.02)
+    span = ctx_len + (cycles + 2) * (D + 1) + 16
+    nblk = (span + 15) // 16
+    tables = np.arange(1, batch * nblk + 1, dtype=np.int32).reshape(batch, nblk)
+    tpool = nmx.KVPool(target, batch * nblk + 2)
+    dpool = nmx.KVPool(draft, batch * nblk + 2)
+    rng = np.random.default_rng(0)
+    last0 = rng.integers(0, tcfg.vocab, batch).astype(np.int32)
+    oracle = None
+    if oracle_draft:
+        # drafts the target's verify accepts in full: start from its greedy
+        # decode, then re-verify until every draft of every cycle is the
+        # verify forward's own greedy id (each round fixes at least one more
+        # position; the kernels are deterministic, so the timed run replays it)
+        guess = target.decode_greedy(tpool, last0, [ctx_len] * batch, tables, cycles * (D + 1) + 1)
+        oracle = []
+        last = last0.copy()
+        pos = np.full(batch, ctx_len, np.int64)
+        for c in range(cycles + 1):
+            dr = [guess[(D + 1) * c:(D + 1) * c + D, b].tolist() for b in range(batch)]
+            for _ in range(D + 1):
+                res = nmx.spec_verify(target, tpool, [dict(last_token=int(last[b]), drafts=dr[b], start_pos=int(pos[b]),
+                                                           block_table=tables[b]) for b in range(batch)],
+                                      nmx.VERIFY_PREFIX)
+                if all(acc == D for _, acc in res):
+                    break
+                dr = [(toks + dr[b][len(toks):])[:D] for b, (toks, acc) in enumerate(res)]
+            oracle.append(dr)
+            for b, (toks, acc) in enumerate(res):
+                pos[b] += 1 + acc
+                last[b] = toks[-1]
+    torch.cuda.synchronize()
+
+    def run(n_cycles, record):
+        last = last0.copy()
+        pos = np.full(batch, ctx_len, np.int64)
+        emitted = accepted = 0
+        t0 = time.perf_counter()
+        for c in range(n_cycles):
+            d = draft.decode_greedy(dpool, last, pos.tolist(), tables, D)  # [D, B]
+            seqs = []
+            for b in range(batch):
+                dr = oracle[c][b] if oracle is not None else d[:, b].tolist()
+                seqs.append(dict(last_token=int(last[b]), drafts=dr, start_pos=int(pos[b]), block_table=tables[b]))
+            res = nmx.spec_verify(target, tpool, seqs, nmx.VERIFY_PREFIX)
+            for b, (toks, acc) in enumerate(res):
+                emitted += len(toks)
+                accepted += acc
+                pos[b] += 1 + acc
+                last[b] = toks[-1]
+        torch.cuda.synchronize()
+        return time.perf_counter() - t0, emitted, accepted
+
+    if oracle is None:
+        run(1, False)  # warm-up: graphs and kernel attributes (the oracle rounds warmed up otherwise)
+    wall, emitted, accepted = run(cycles, True)
+    return {"what": "speculative decoding", "target_layers": layers, "draft_layers": draft_layers, "batch": batch,
+            "ctx": ctx_len, "drafts": D, "cycles": cycles, "oracle_draft": bool(oracle_draft),
+            "ms_per_cycle": round(wall * 1000.0 / cycles, 3), "tok_s": round(emitted / wall, 1),
+            "acceptance": round(accepted / (cycles * batch * D), 4),
+            "target_weight_bytes": target.step_weight_bytes, "draft_weight_bytes": draft.step_weight_bytes}
+
+
 def main():
     import torch
 
     from novamlx_b200 import nmx
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemv", "gemm", "attn", "decode", "serve"])
+    ap.add_argument("what", choices=["gemv", "gemm", "attn", "decode", "serve", "spec"])
     ap.add_argument("--n", type=int, default=None, help="gemv: 28672, gemm: 4096")
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--m", type=int, default=None, help="gemv: 1, gemm: 2048")
@@ -213,11 +297,15 @@ def main():
     ap.add_argument("--seqs", type=int, default=64)
     ap.add_argument("--step-tokens", type=int, default=4096)
     ap.add_argument("--chunk", type=int, default=512)
+    ap.add_argument("--drafts", type=int, default=4)
+    ap.add_argument("--cycles", type=int, default=8)
+    ap.add_argument("--draft-layers", type=int, default=16)
+    ap.add_argument("--oracle-draft", action="store_true")
     a = ap.parse_args()
     if a.copies is None:
         a.copies = 1 if a.what == "gemm" else 3
     if a.layers is None:
-        a.layers = 32 if a.what == "serve" else 2
+        a.layers = {"serve": 32, "spec": 80}.get(a.what, 2)
     if a.tokens is None:
         a.tokens = 256 if a.what == "serve" else 64
     if a.n is None:
@@ -233,6 +321,9 @@ def main():
             r = gemm(c, torch, a.m, a.n, a.k, a.reps, a.copies)
         elif a.what == "attn":
             r = attn(c, torch, a.batch, a.ctx, a.reps)
+        elif a.what == "spec":
+            r = spec(c, torch, nmx, a.batch if a.batch != 1 else 16, a.ctx if a.ctx != 2048 else 4096, a.drafts,
+                     a.cycles, a.layers, a.draft_layers, a.oracle_draft)
         elif a.what == "serve":
             r = serve(c, torch, nmx, a.layers, a.seqs, a.tokens, a.step_tokens, a.chunk)
         else:

@@ -139,6 +139,23 @@ _proto("nmx_sched_step", _i, _vp, C.POINTER(C.c_int))
 _proto("nmx_sched_poll", _i, _vp, C.c_int64, _vp, _i, C.POINTER(C.c_int), C.POINTER(C.c_int))
 _proto("nmx_sched_stats", _i, _vp, C.POINTER(SchedStats))
 REQ_WAITING, REQ_PREFILL, REQ_DECODE, REQ_DONE, REQ_PREEMPTED = range(5)
+
+
+class SpecSeq(C.Structure):
+    _fields_ = [("last_token", C.c_int32), ("drafts", C.POINTER(C.c_int32)), ("n_drafts", C.c_int),
+                ("start_pos", C.c_int), ("block_table", C.POINTER(C.c_int32)), ("n_blocks", C.c_int)]
+
+
+_proto("nmx_ngram_create", _i, _i, _i, _i, _i, C.POINTER(_vp))
+_proto("nmx_ngram_destroy", None, _vp)
+_proto("nmx_ngram_record_token", None, _vp, C.c_int32)
+_proto("nmx_ngram_record_tokens", None, _vp, C.POINTER(C.c_int32), _i)
+_proto("nmx_ngram_speculate", _i, _vp, C.POINTER(C.c_int32), _i, C.POINTER(C.c_int32), _i)
+_proto("nmx_ngram_record_accepted", None, _vp, C.POINTER(C.c_int32), _i, _i)
+_proto("nmx_ngram_stats", None, _vp, C.POINTER(_i), C.POINTER(C.c_longlong), C.POINTER(_i), C.POINTER(C.c_double))
+_proto("nmx_spec_verify", _i, _vp, _vp, C.POINTER(SpecSeq), _i, _i, C.POINTER(C.c_int32), C.POINTER(_i),
+       C.POINTER(_i))
+VERIFY_NGRAM, VERIFY_PREFIX = 0, 1
 _proto("nmx_block_pool_destroy", None, _vp)
 _proto("nmx_block_pool_allocate", _i, _vp)
 _proto("nmx_block_pool_free", None, _vp, _i)
@@ -412,6 +429,27 @@ def llama31_8b(**kw) -> ModelConfig:
     base = dict(vocab=128256, hidden=4096, n_layers=32, n_heads=32, n_kv_heads=8, head_dim=128, ffn=14336,
                 rms_eps=1e-5, rope_theta=500000.0, rope_factor=8.0, rope_low_freq_factor=1.0,
                 rope_high_freq_factor=4.0, rope_original_max_pos=8192)
+    base.update(kw)
+    return ModelConfig(**base)
+
+
+def llama33_70b(**kw) -> ModelConfig:
+    """Llama-3.3-70B-style architecture (hidden 8192, 80 layers, 64/8 heads, ffn 28672, vocab 128256,
+    RoPE θ 5e5 with the llama3 scaling)."""
+    base = dict(vocab=128256, hidden=8192, n_layers=80, n_heads=64, n_kv_heads=8, head_dim=128, ffn=28672,
+                rms_eps=1e-5, rope_theta=500000.0, rope_factor=8.0, rope_low_freq_factor=1.0,
+                rope_high_freq_factor=4.0, rope_original_max_pos=8192)
+    base.update(kw)
+    return ModelConfig(**base)
+
+
+def llama32_1b(**kw) -> ModelConfig:
+    """Llama-3.2-1B-style draft architecture (hidden 2048, 16 layers, 32/8 heads of 64, ffn 8192,
+    vocab 128256). The original ties the output head to the embedding; here the head is its own
+    quantized [vocab, hidden] matrix, which streams the same bytes per token."""
+    base = dict(vocab=128256, hidden=2048, n_layers=16, n_heads=32, n_kv_heads=8, head_dim=64, ffn=8192,
+                rms_eps=1e-5, rope_theta=500000.0, rope_factor=32.0,
+                rope_low_freq_factor=1.0, rope_high_freq_factor=4.0, rope_original_max_pos=8192)
     base.update(kw)
     return ModelConfig(**base)
 
@@ -742,3 +780,70 @@ class Scheduler:
         if _finalizing():
             return
         self.close()
+
+
+class NGramSpeculator:
+    """nmx_ngram_t: NGramSpeculator + SpeculativeDecoder's acceptance count."""
+
+    def __init__(self, ngram_size: int = 4, max_draft: int = 5, min_hits: int = 1, max_cache_size: int = 65536):
+        h = _vp()
+        check(lib.nmx_ngram_create(ngram_size, max_draft, min_hits, max_cache_size, C.byref(h)))
+        self.h = h
+        self.max_draft = max_draft
+
+    def record_token(self, token: int):
+        lib.nmx_ngram_record_token(self.h, int(token))
+
+    def record_tokens(self, tokens):
+        t = _i32(tokens)
+        lib.nmx_ngram_record_tokens(self.h, _iptr(t), len(t))
+
+    def speculate(self, context=None):
+        out = np.zeros(max(self.max_draft, 1), np.int32)
+        if context is None:
+            n = lib.nmx_ngram_speculate(self.h, None, 0, _iptr(out), len(out))
+        else:
+            c = _i32(context)
+            n = lib.nmx_ngram_speculate(self.h, _iptr(c), len(c), _iptr(out), len(out))
+        return [int(v) for v in out[:n]]
+
+    def record_accepted(self, tokens, accepted: int):
+        t = _i32(tokens)
+        lib.nmx_ngram_record_accepted(self.h, _iptr(t), len(t), int(accepted))
+
+    @property
+    def stats(self):
+        cs, hits, buf, rate = C.c_int(), C.c_longlong(), C.c_int(), C.c_double()
+        lib.nmx_ngram_stats(self.h, C.byref(cs), C.byref(hits), C.byref(buf), C.byref(rate))
+        return {"cache_size": cs.value, "total_hits": hits.value, "buffer_size": buf.value,
+                "acceptance_rate": rate.value}
+
+    def __del__(self, _finalizing=sys.is_finalizing):
+        if not _finalizing() and getattr(self, "h", None):
+            lib.nmx_ngram_destroy(self.h)
+            self.h = None
+
+
+def spec_verify(model: Model, pool: KVPool, seqs, rule: int = VERIFY_PREFIX):
+    """nmx_spec_verify over dicts {last_token, drafts, start_pos, block_table};
+    returns [(tokens, accepted)] per sequence."""
+    keep = []
+    arr = (SpecSeq * len(seqs))()
+    max_d = 0
+    for i, sq in enumerate(seqs):
+        d = _i32(sq.get("drafts", []))
+        t = _i32(sq["block_table"])
+        keep += [d, t]
+        arr[i].last_token = int(sq["last_token"])
+        arr[i].drafts = _iptr(d)
+        arr[i].n_drafts = len(d)
+        arr[i].start_pos = int(sq["start_pos"])
+        arr[i].block_table = _iptr(t)
+        arr[i].n_blocks = len(t)
+        max_d = max(max_d, len(d))
+    out = np.zeros((len(seqs), max_d + 1), np.int32)
+    cnt = np.zeros(len(seqs), np.int32)
+    acc = np.zeros(len(seqs), np.int32)
+    check(lib.nmx_spec_verify(model.h, pool.h, arr, len(seqs), int(rule), _iptr(out),
+                              cnt.ctypes.data_as(C.POINTER(_i)), acc.ctypes.data_as(C.POINTER(_i))))
+    return [(out[i, :cnt[i]].tolist(), int(acc[i])) for i in range(len(seqs))]
