@@ -450,6 +450,35 @@ NMX_API nmx_status_t nmx_sched_poll(nmx_sched_t sched, int64_t request_id, int32
 NMX_API nmx_status_t nmx_sched_stats(nmx_sched_t sched, nmx_sched_stats_t* out);
 
 /* ------------------------------------------------------------------------ */
+/* Tensor parallelism (one process per GPU). Each rank creates the model of
+ * its shard: n_heads / t and n_kv_heads / t heads, ffn / t, and loads the
+ * matching rows of q/k/v/gate/up (and q/k/v biases) and the matching K
+ * columns (words, scales, biases) of o_proj / down_proj; embeddings, norms
+ * and the LM head are replicated. A communicator joins the ranks' block
+ * outputs: after o_proj and after down_proj every rank computes
+ * h = h + sum over ranks of the partial products, by one kernel reading the
+ * peers' partials over NVLink (CUDA IPC, plain peer loads and stores, no
+ * collective library). Setup: nmx_comm_create on every rank, exchange the
+ * NMX_IPC_HANDLE_BYTES handles (any host rendezvous), nmx_comm_connect with
+ * all of them in rank order, nmx_model_set_comm. Every rank must then run the
+ * same sequence of forwards. Replaces the sharded model the north star's
+ * 32B/70B configurations call for (no counterpart in the single-device
+ * reference engine). */
+#define NMX_IPC_HANDLE_BYTES 64
+typedef struct nmx_comm_s* nmx_comm_t;
+/* region_bytes: at least max_tokens x hidden x 2 of the models it serves */
+NMX_API nmx_status_t nmx_comm_create(nmx_ctx_t ctx, int rank, int world, size_t region_bytes, nmx_comm_t* out);
+NMX_API nmx_status_t nmx_comm_ipc_handle(nmx_comm_t comm, void* out_handle);
+NMX_API nmx_status_t nmx_comm_connect(nmx_comm_t comm, const void* handles /* world x NMX_IPC_HANDLE_BYTES */);
+NMX_API void nmx_comm_destroy(nmx_comm_t comm);
+/* NULL detaches. Clears the model's captured decode graphs. */
+NMX_API nmx_status_t nmx_model_set_comm(nmx_model_t model, nmx_comm_t comm);
+/* out[rows, cols] = res + sum over ranks of every rank's partial (f16, rank
+ * order); every rank calls it with its own partial. */
+NMX_API nmx_status_t nmx_op_allreduce_resid(nmx_comm_t comm, const void* partial, int rows, int cols, const void* res,
+                                            void* out);
+
+/* ------------------------------------------------------------------------ */
 /* Speculative decoding. */
 
 /* N-gram draft source (NGramSpeculator, Sources/NovaMLXEngine/CompiledSampler.swift:60-204,

@@ -555,6 +555,16 @@ nmx_status_t Model::linear(const Lin& l, const void* x, long ldx, const void* ga
   return qgemv(ctx, a, cfg.bits, cfg.group_size, dt, epi);
 }
 
+// o_proj / down_proj: h += x · Wᵀ. Under tensor parallelism this rank's
+// partial (its K shard) goes to the communicator's region and the exchange
+// kernel writes h = h + Σ_ranks partial on every rank.
+nmx_status_t Model::block_out(const Lin& l, const void* x, long ldx, int M, int region) {
+  const int H = cfg.hidden;
+  if (!comm) return linear(l, x, ldx, nullptr, M, H, 0, nullptr, h, H, h, H, EPI_RESID);
+  NMX_TRY(linear(l, x, ldx, nullptr, M, H, 0, nullptr, comm_region(comm, region), H, nullptr, 0, EPI_STORE));
+  return comm_allreduce_resid(comm, region, M, H, h, H, h, H, ctx->dev_err);
+}
+
 nmx_status_t Model::run_layers_decode(KvPool* pool, int B) {
   Ctx* c = ctx;
   const nmx_model_cfg& cf = cfg;
@@ -577,11 +587,11 @@ nmx_status_t Model::run_layers_decode(KvPool* pool, int B) {
     at.kv_static = true;
     NMX_TRY(paged_attention(c, at, true));
 
-    NMX_TRY(linear(ly.o, attn, Nq, nullptr, B, H, 0, nullptr, h, H, h, H, EPI_RESID));
+    NMX_TRY(block_out(ly.o, attn, Nq, B, 0));
 
     NMX_TRY(linear(ly.gu, h, H, ly.mlp_norm, B, F, F, nullptr, act, F, nullptr, 0, EPI_SILU));
 
-    NMX_TRY(linear(ly.down, act, F, nullptr, B, H, 0, nullptr, h, H, h, H, EPI_RESID));
+    NMX_TRY(block_out(ly.down, act, F, B, 1));
   }
   return NMX_OK;
 }
@@ -607,11 +617,11 @@ nmx_status_t Model::run_layers_prefill(KvPool* pool, int T) {
     at.splits = 1; at.scale = 1.0f / std::sqrt(float(cf.head_dim));
     NMX_TRY(paged_attention(c, at, false));
 
-    NMX_TRY(linear(ly.o, attn, Nq, nullptr, T, H, 0, nullptr, h, H, h, H, EPI_RESID));
+    NMX_TRY(block_out(ly.o, attn, Nq, T, 0));
 
     NMX_TRY(linear(ly.gu, h, H, ly.mlp_norm, T, F, F, nullptr, act, F, nullptr, 0, EPI_SILU));
 
-    NMX_TRY(linear(ly.down, act, F, nullptr, T, H, 0, nullptr, h, H, h, H, EPI_RESID));
+    NMX_TRY(block_out(ly.down, act, F, T, 1));
   }
   return NMX_OK;
 }
@@ -819,6 +829,7 @@ int phase_ctas(int num_sms, int n_tg, int K) {
 
 bool Model::persistent_ok(int B) const {
   if (!persistent_enabled || persistent_unusable || B != 1 || (!weights_ready && !loaded_any)) return false;
+  if (comm) return false;  // the persistent schedule has no exchange phase
   const nmx_model_cfg& cf = cfg;
   const int rep = cf.n_kv_heads > 0 ? cf.n_heads / cf.n_kv_heads : 0;
   if (!(cf.head_dim == 64 || cf.head_dim == 128) || rep < 1 || rep > 8 || cf.hidden % 8 != 0) return false;

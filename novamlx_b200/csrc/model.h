@@ -37,6 +37,8 @@ struct GraphEntry {
 
 struct KvPool;
 
+struct Comm;
+
 struct Model {
   Ctx* ctx = nullptr;
   nmx_model_cfg cfg{};
@@ -70,6 +72,11 @@ struct Model {
   int pool_blocks_hint = 0;
   size_t h2d_bytes_last = 0;
   std::map<std::pair<int, const void*>, GraphEntry> graphs;
+  void graphs_clear() {
+    for (auto& g : graphs)
+      if (g.second.exec) cudaGraphExecDestroy(g.second.exec);
+    graphs.clear();
+  }
 
   // set by resolve() when the named part lives inside decode records
   Lin* rs_lin = nullptr;
@@ -97,6 +104,7 @@ struct Model {
   nmx_status_t linear(const Lin& l, const void* x, long ldx, const void* gamma, int M, int N_out,
                       long pair_off_rows, const void* bias, void* y, long ldy, const void* res, long ldres,
                       int epi, float* logits_f32 = nullptr, int* ids = nullptr, int* next_tokens = nullptr);
+  nmx_status_t block_out(const Lin& l, const void* x, long ldx, int M, int region);
   nmx_status_t run_layers_decode(KvPool* pool, int B);
   nmx_status_t run_layers_prefill(KvPool* pool, int T);
   nmx_status_t run_head(const void* x, int rows, bool want_logits, int* next_tokens);
@@ -106,6 +114,10 @@ struct Model {
   nmx_status_t forward(KvPool* pool, const nmx_seq_t* seqs, int n, nmx_out_mode_t mode, void* out_host);
   nmx_status_t finish_step();
   // persistent batch-1 decode (decode_persistent.cu)
+  // tensor parallelism: this rank's shard of every linear; o/down partials
+  // are exchanged and summed (with the residual) through the communicator
+  Comm* comm = nullptr;
+  nmx_comm_s* comm_handle = nullptr;
   bool persistent_enabled = false;  // opt-in: the per-layer graph is faster today
   bool persistent_unusable = false;  // the device refused the launch (cooperative / shared memory)
   PPhase* pers_ph = nullptr;
@@ -120,6 +132,13 @@ struct Model {
   nmx_status_t decode_greedy(KvPool* pool, const int32_t* first, const int32_t* start, const int32_t* tables,
                              int max_blocks, int n, int steps, int32_t* out_host);
 };
+
+struct Comm;
+size_t comm_region_bytes(const Comm* c);
+void* comm_region(Comm* c, int r);
+// out = res + sum over ranks (rank order) of every rank's region r rows
+nmx_status_t comm_allreduce_resid(Comm* cm, int region, int rows, int cols, const void* res, long ldres, void* out,
+                                  long ldo, unsigned* err);
 
 struct KvPool {
   Model* model = nullptr;

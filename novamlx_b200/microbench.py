@@ -6,6 +6,7 @@
   python -m novamlx_b200.microbench decode [--layers 2] [--ctx 2048] [--tokens 64] [--batch 1]
   python -m novamlx_b200.microbench serve [--layers 32] [--seqs 64] [--tokens 256]
   python -m novamlx_b200.microbench spec [--batch 16] [--ctx 4096] [--drafts 4] [--cycles 8] [--oracle-draft]
+  torchrun --nproc-per-node T -m novamlx_b200.microbench tp [--batch 32] [--ctx 8192] [--steps 16] [--prefill 8192]
 
 gemv: the decode-record GEMV (nmx_op_qmatmul_records) over `copies` distinct
 weight copies, so the weights come from HBM on every launch.
@@ -40,6 +41,13 @@ own greedy continuation (computed before the timed cycles) for the
 full-acceptance verify throughput. The pages before --ctx are left as
 allocated (zeros): the timed work, reading ctx positions of K/V per row, is
 the same as after a real prefill.
+
+tp: tensor-parallel decode of the Qwen2.5-32B-style architecture (random
+4-bit weights, --layers layers) over the ranks of torch.distributed.run (one
+GPU each; T = 1 runs without the exchange): batch --batch at context --ctx
+(pages before --ctx left as allocated), --steps greedy steps timed with CUDA
+events on every rank, the maximum taken; optionally one --prefill-token
+prefill of a single sequence, timed the same way.
 
 Prints one JSON line per run with the average launch duration measured by
 CUDA events on the library's stream and the algorithmic bytes per launch.
@@ -278,13 +286,72 @@ def spec(ctx, torch, nmx, batch, ctx_len, n_drafts, cycles, layers, draft_layers
             "target_weight_bytes": target.step_weight_bytes, "draft_weight_bytes": draft.step_weight_bytes}
 
 
+def tp(torch, nmx, batch, ctx_len, steps, layers, prefill):
+    import numpy as np
+    import os
+    import torch.distributed as dist
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        dist.init_process_group("gloo", init_method="env://")
+    torch.cuda.set_device(rank)
+    ctx = nmx.Context(rank)
+    max_tokens = max(batch, prefill or 0, 16)
+    cfg = nmx.qwen25_32b(n_layers=layers, max_batch=batch, max_tokens=max_tokens)
+    local = nmx.tp_config(cfg, world)
+    m = nmx.Model(ctx, local)
+    m.init_random(seed=rank, std=0.02)
+    comm = None
+    if world > 1:
+        comm = nmx.tp_comm(ctx, rank, world, max_tokens * cfg.hidden * 2, nmx.torch_exchange(dist))
+        m.set_comm(comm)
+    nblk = (ctx_len + steps + 64 + 15) // 16
+    pblk = ((prefill or 0) + 15) // 16
+    pool = nmx.KVPool(m, batch * nblk + pblk + 2)
+    tables = np.arange(1, batch * nblk + 1, dtype=np.int32).reshape(batch, nblk)
+    first = np.random.default_rng(0).integers(0, cfg.vocab, batch).astype(np.int32)
+
+    def timed(fn):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(ctx.stream):
+            e0.record()
+            fn()
+            e1.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([e0.elapsed_time(e1)])
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        return float(ms[0])
+
+    m.decode_greedy(pool, first, [ctx_len] * batch, tables, 4, want_ids=False)  # graphs, attributes
+    ms = timed(lambda: m.decode_greedy(pool, first, [ctx_len] * batch, tables, steps, want_ids=False))
+    out = {"what": "tensor-parallel decode", "model": "qwen2.5-32b-style", "layers": layers, "tp": world,
+           "batch": batch, "ctx": ctx_len, "steps": steps, "ms_per_step": round(ms / steps, 3),
+           "tok_s": round(batch * steps * 1000.0 / ms, 1),
+           "weight_bytes_per_rank": m.step_weight_bytes, "kv_bytes_per_token_per_rank": m.kv_bytes_per_token}
+    if prefill:
+        ptab = np.arange(batch * nblk + 1, batch * nblk + 1 + pblk, dtype=np.int32)
+        ptoks = np.random.default_rng(1).integers(0, cfg.vocab, prefill)
+        m.forward(pool, [dict(tokens=ptoks[:256], start_pos=0, block_table=ptab)])  # warm
+        pm = timed(lambda: m.forward(pool, [dict(tokens=ptoks, start_pos=0, block_table=ptab)]))
+        out.update(prefill_tokens=prefill, prefill_ms=round(pm, 2))
+    if world > 1:
+        m.set_comm(None)
+        comm.close()
+        dist.barrier()
+        dist.destroy_process_group()
+    return out if rank == 0 else None
+
+
 def main():
     import torch
 
     from novamlx_b200 import nmx
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemv", "gemm", "attn", "decode", "serve", "spec"])
+    ap.add_argument("what", choices=["gemv", "gemm", "attn", "decode", "serve", "spec", "tp"])
     ap.add_argument("--n", type=int, default=None, help="gemv: 28672, gemm: 4096")
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--m", type=int, default=None, help="gemv: 1, gemm: 2048")
@@ -301,17 +368,25 @@ def main():
     ap.add_argument("--cycles", type=int, default=8)
     ap.add_argument("--draft-layers", type=int, default=16)
     ap.add_argument("--oracle-draft", action="store_true")
+    ap.add_argument("--steps", type=int, default=16)
+    ap.add_argument("--prefill", type=int, default=0)
     a = ap.parse_args()
     if a.copies is None:
         a.copies = 1 if a.what == "gemm" else 3
     if a.layers is None:
-        a.layers = {"serve": 32, "spec": 80}.get(a.what, 2)
+        a.layers = {"serve": 32, "spec": 80, "tp": 64}.get(a.what, 2)
     if a.tokens is None:
         a.tokens = 256 if a.what == "serve" else 64
     if a.n is None:
         a.n = 4096 if a.what == "gemm" else 28672
     if a.m is None:
         a.m = 2048 if a.what == "gemm" else 1
+    if a.what == "tp":
+        r = tp(torch, nmx, a.batch if a.batch != 1 else 32, a.ctx if a.ctx != 2048 else 8192, a.steps, a.layers,
+               a.prefill)
+        if r is not None:
+            print(json.dumps(r), flush=True)
+        return
     torch.cuda.set_device(0)
     c = nmx.Context(0)
     with torch.cuda.stream(c.stream):

@@ -156,6 +156,13 @@ _proto("nmx_ngram_stats", None, _vp, C.POINTER(_i), C.POINTER(C.c_longlong), C.P
 _proto("nmx_spec_verify", _i, _vp, _vp, C.POINTER(SpecSeq), _i, _i, C.POINTER(C.c_int32), C.POINTER(_i),
        C.POINTER(_i))
 VERIFY_NGRAM, VERIFY_PREFIX = 0, 1
+IPC_HANDLE_BYTES = 64
+_proto("nmx_comm_create", _i, _vp, _i, _i, _sz, C.POINTER(_vp))
+_proto("nmx_comm_ipc_handle", _i, _vp, _vp)
+_proto("nmx_comm_connect", _i, _vp, _vp)
+_proto("nmx_comm_destroy", None, _vp)
+_proto("nmx_model_set_comm", _i, _vp, _vp)
+_proto("nmx_op_allreduce_resid", _i, _vp, _vp, _i, _i, _vp, _vp)
 _proto("nmx_block_pool_destroy", None, _vp)
 _proto("nmx_block_pool_allocate", _i, _vp)
 _proto("nmx_block_pool_free", None, _vp, _i)
@@ -489,6 +496,11 @@ class Model:
 
     def init_random(self, seed: int = 0, std: float = 0.02):
         check(lib.nmx_model_init_random(self.h, seed, std))
+
+    def set_comm(self, comm: Optional["Comm"]):
+        """tensor parallelism: join o_proj / down_proj outputs over the ranks"""
+        check(lib.nmx_model_set_comm(self.h, comm.h if comm is not None else None))
+        self.comm = comm  # keep it alive while the model uses it
 
     def load_tensor(self, name: str, arr: np.ndarray):
         arr = np.ascontiguousarray(arr)
@@ -847,3 +859,99 @@ def spec_verify(model: Model, pool: KVPool, seqs, rule: int = VERIFY_PREFIX):
     check(lib.nmx_spec_verify(model.h, pool.h, arr, len(seqs), int(rule), _iptr(out),
                               cnt.ctypes.data_as(C.POINTER(_i)), acc.ctypes.data_as(C.POINTER(_i))))
     return [(out[i, :cnt[i]].tolist(), int(acc[i])) for i in range(len(seqs))]
+
+
+class Comm:
+    """nmx_comm_t: this rank's end of the tensor-parallel exchange (peer
+    partials over CUDA IPC)."""
+
+    def __init__(self, ctx: Context, rank: int, world: int, region_bytes: int):
+        h = _vp()
+        check(lib.nmx_comm_create(ctx.h, rank, world, region_bytes, C.byref(h)))
+        self.h, self.ctx, self.rank, self.world = h, ctx, rank, world
+
+    def handle(self) -> bytes:
+        buf = (C.c_ubyte * IPC_HANDLE_BYTES)()
+        check(lib.nmx_comm_ipc_handle(self.h, buf))
+        return bytes(buf)
+
+    def connect(self, handles):
+        assert len(handles) == self.world and all(len(b) == IPC_HANDLE_BYTES for b in handles)
+        blob = b"".join(handles)
+        buf = (C.c_ubyte * len(blob)).from_buffer_copy(blob)
+        check(lib.nmx_comm_connect(self.h, buf))
+
+    def allreduce_resid(self, partial, res, out):
+        """out = res + sum over ranks of partial (device tensors, [rows, cols] f16)"""
+        rows, cols = partial.shape
+        check(self.ctx._op(lambda: lib.nmx_op_allreduce_resid(self.h, partial.data_ptr(), rows, cols, res.data_ptr(),
+                                                              out.data_ptr())))
+        return out
+
+    def close(self):
+        if self.h:
+            lib.nmx_comm_destroy(self.h)
+            self.h = None
+
+    def __del__(self, _finalizing=sys.is_finalizing):
+        if not _finalizing():
+            self.close()
+
+
+def tp_comm(ctx: Context, rank: int, world: int, region_bytes: int, exchange) -> Comm:
+    """Create this rank's communicator and connect it; exchange(bytes) must
+    return every rank's bytes in rank order (e.g. torch.distributed
+    all_gather_object)."""
+    comm = Comm(ctx, rank, world, region_bytes)
+    comm.connect(exchange(comm.handle()))
+    return comm
+
+
+def torch_exchange(dist):
+    """exchange() over an initialised torch.distributed process group"""
+    def ex(b: bytes):
+        out = [None] * dist.get_world_size()
+        dist.all_gather_object(out, b)
+        return out
+    return ex
+
+
+def tp_config(cfg: ModelConfig, world: int) -> ModelConfig:
+    """The model config of one tensor-parallel rank: heads and ffn split."""
+    import dataclasses
+    if cfg.n_heads % world or cfg.n_kv_heads % world or cfg.ffn % world:
+        raise ValueError("heads, kv heads and ffn must divide by the tensor-parallel size")
+    if (cfg.ffn // world) % cfg.group_size or (cfg.n_heads // world * cfg.head_dim) % cfg.group_size:
+        raise ValueError("a rank's K shard of o_proj / down_proj must be whole quantization groups")
+    return dataclasses.replace(cfg, n_heads=cfg.n_heads // world, n_kv_heads=cfg.n_kv_heads // world,
+                               ffn=cfg.ffn // world)
+
+
+def tp_shard(tensors: dict, cfg: ModelConfig, rank: int, world: int) -> dict:
+    """This rank's slice of MLX-layout tensors (names unchanged): rows of
+    q/k/v/gate/up (and q/k/v biases), K columns of o/down (packed words,
+    scales, biases); everything else replicated."""
+    D, bits, gs = cfg.head_dim, cfg.bits, cfg.group_size
+    nq, nkv, f = cfg.n_heads // world * D, cfg.n_kv_heads // world * D, cfg.ffn // world
+    per_word = 32 // bits
+    out = {}
+    for name, t in tensors.items():
+        parts = name.split(".")
+        kind = parts[-1]  # weight | scales | biases | bias
+        mod = parts[-2] if len(parts) >= 2 else ""
+        rows = {"q_proj": nq, "k_proj": nkv, "v_proj": nkv, "gate_proj": f, "up_proj": f}.get(mod)
+        cols = {"o_proj": nq, "down_proj": f}.get(mod)
+        if rows is not None:
+            out[name] = np.ascontiguousarray(t[rank * rows:(rank + 1) * rows])
+        elif cols is not None:
+            if kind == "weight":
+                w = cols // per_word
+            elif kind in ("scales", "biases"):
+                w = cols // gs
+            else:
+                out[name] = t
+                continue
+            out[name] = np.ascontiguousarray(t[:, rank * w:(rank + 1) * w])
+        else:
+            out[name] = t
+    return out

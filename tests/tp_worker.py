@@ -1,0 +1,90 @@
+"""One rank of the tensor-parallel parity check (test infrastructure; run
+under torch.distributed.run by tests/test_tp.py). Every rank loads its shard
+of the same tiny model, joins the communicator, and runs a ragged prefill, a
+batched decode step and a device greedy loop; rank 0 also runs the unsharded
+model on its GPU and writes both results to the output file."""
+import argparse
+import os
+import sys
+
+import numpy as np
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def tiny(name):
+    llama = dict(vocab=1024, hidden=512, n_layers=2, n_heads=8, n_kv_heads=2, head_dim=64, ffn=1024,
+                 rope_theta=500000.0, rope_factor=8.0, rope_low_freq_factor=1.0, rope_high_freq_factor=4.0,
+                 rope_original_max_pos=64, rms_eps=1e-5)
+    qwen = dict(vocab=1024, hidden=512, n_layers=2, n_heads=4, n_kv_heads=2, head_dim=128, ffn=1536,
+                qkv_bias=True, rope_theta=1e6, rms_eps=1e-6)
+    return {"llama": llama, "qwen": qwen}[name]
+
+
+def run(nmx, m, pool, rng_seed, cfg):
+    rng = np.random.default_rng(rng_seed)
+    lens = [3, 40, 17, 70]
+    prompts = [rng.integers(0, cfg.vocab, n) for n in lens]
+    tables = [np.arange(8 * i + 1, 8 * i + 9, dtype=np.int32) for i in range(4)]
+    logits = m.forward(pool, [dict(tokens=p, start_pos=0, block_table=t) for p, t in zip(prompts, tables)],
+                       nmx.OUT_LOGITS_LAST)
+    first = m.forward(pool, [dict(tokens=p, start_pos=0, block_table=t) for p, t in zip(prompts, tables)])
+    ids = m.decode_greedy(pool, first, lens, np.stack(tables), 6)
+    return logits, first, ids
+
+
+def main():
+    import torch
+    import torch.distributed as dist
+    from oracle import oracle as O
+    from novamlx_b200 import nmx
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", default="llama")
+    ap.add_argument("--out", required=True)
+    a = ap.parse_args()
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dist.init_process_group("gloo", init_method="env://")
+    torch.cuda.set_device(rank)
+    d = tiny(a.model)
+    full_cfg = nmx.ModelConfig(**d, max_batch=8, max_tokens=256)
+    tensors = O.random_tensors(O.TinyCfg(**d), seed=5, std=0.05)
+    shard = nmx.tp_shard(tensors, full_cfg, rank, world)
+    ctx = nmx.Context(rank)
+    m = nmx.Model(ctx, nmx.tp_config(full_cfg, world))
+    for k, v in shard.items():
+        m.load_tensor(k, v.view(np.float16) if v.dtype == np.uint16 else v)
+    comm = nmx.tp_comm(ctx, rank, world, full_cfg.max_tokens * full_cfg.hidden * 2, nmx.torch_exchange(dist))
+    m.set_comm(comm)
+    pool = nmx.KVPool(m, 40)
+
+    # op-level exchange: rank r contributes (r + 1) * base
+    base = torch.arange(64 * 512, device=f"cuda:{rank}", dtype=torch.float32).reshape(64, 512) % 7 - 3
+    part = ((rank + 1) * base).half()
+    res = torch.ones_like(part)
+    out = torch.empty_like(part)
+    comm.allreduce_resid(part, res, out)
+    torch.cuda.synchronize()
+    ctx.synchronize()
+    expect = (1 + base * sum(range(1, world + 1))).half()
+    op_ok = bool(torch.equal(out, expect))
+
+    tp_logits, tp_first, tp_ids = run(nmx, m, pool, 11, full_cfg)
+    dist.barrier()
+    m.set_comm(None)
+    comm.close()
+    result = dict(op_ok=np.array(op_ok), tp_logits=tp_logits, tp_first=tp_first, tp_ids=tp_ids)
+    if rank == 0:
+        fm = nmx.Model(ctx, full_cfg)
+        for k, v in tensors.items():
+            fm.load_tensor(k, v.view(np.float16) if v.dtype == np.uint16 else v)
+        fpool = nmx.KVPool(fm, 40)
+        f_logits, f_first, f_ids = run(nmx, fm, fpool, 11, full_cfg)
+        result.update(full_logits=f_logits, full_first=f_first, full_ids=f_ids)
+    np.savez(f"{a.out}.rank{rank}.npz", **result)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
