@@ -135,6 +135,20 @@ NMX_API nmx_status_t nmx_op_rmsnorm(nmx_ctx_t ctx, const void* x, const void* ga
 NMX_API nmx_status_t nmx_op_argmax(nmx_ctx_t ctx, const void* logits, int M, int V,
                                    nmx_dtype_t dtype, int32_t* out);
 
+/* Sampling beyond greedy, per row of logits (dtype f16/bf16/f32), all
+ * outputs in device memory: temperature 0 → argmax; otherwise categorical
+ * over logSoftmax(logits) / temperature, restricted to the top-p nucleus when
+ * 0 < top_p < 1 (the tokens whose strictly-higher probability mass is below
+ * top_p, as CompiledSampler keeps them, Sources/NovaMLXEngine/CompiledSampler.swift:28-49).
+ * Draws are a function of (seed, counter, row, token): the same arguments
+ * give the same ids. out_logprob (may be NULL): the chosen id's logprob;
+ * top_k (0..32) largest logprobs and their ids, descending — the data of
+ * computeRawLogprobs, FusedBatchScheduler.swift:900-941. */
+NMX_API nmx_status_t nmx_op_sample(nmx_ctx_t ctx, const void* logits, int M, int V, nmx_dtype_t dtype,
+                                   float temperature, float top_p, uint64_t seed, uint64_t counter,
+                                   int32_t* out_ids, float* out_logprob, int top_k, int32_t* out_top_ids,
+                                   float* out_top_logprobs);
+
 /* Greedy next id with the engine's frequency penalty applied first:
  * logits[m] - penalty * histogram(recent[m, 0:n_recent[m]]) →
  * argmax. recent is int32[M, max_recent]. Mirrors
@@ -448,6 +462,43 @@ NMX_API nmx_status_t nmx_sched_step(nmx_sched_t sched, int* n_generated);
 NMX_API nmx_status_t nmx_sched_poll(nmx_sched_t sched, int64_t request_id, int32_t* out_tokens,
                                     int max_tokens, int* n_tokens, int* state);
 NMX_API nmx_status_t nmx_sched_stats(nmx_sched_t sched, nmx_sched_stats_t* out);
+
+/* ------------------------------------------------------------------------ */
+/* safetensors files: checkpoints and the SSD prefix-block store. */
+typedef struct nmx_safetensors_s* nmx_safetensors_t;
+/* Header checks of SafetensorsHeader.swift:12-31 (length > 0, < 16 MiB),
+ * plus every entry's dtype / shape / offsets. */
+NMX_API nmx_status_t nmx_safetensors_open(const char* path, nmx_safetensors_t* out);
+NMX_API void nmx_safetensors_close(nmx_safetensors_t st);
+NMX_API int nmx_safetensors_count(nmx_safetensors_t st);
+/* name (NUL-terminated, name_cap bytes), dtype ("F16", "U32", ... in 8
+ * bytes), shape (up to 8 dims), ndim, data bytes of tensor i. */
+NMX_API nmx_status_t nmx_safetensors_info(nmx_safetensors_t st, int i, char* name, int name_cap, char* dtype,
+                                          int64_t* shape, int* ndim, uint64_t* nbytes);
+/* __metadata__[key] into out (truncated to cap - 1); returns its length, -1 if absent. */
+NMX_API int nmx_safetensors_metadata(nmx_safetensors_t st, const char* key, char* out, int cap);
+NMX_API nmx_status_t nmx_safetensors_read(nmx_safetensors_t st, const char* name, void* host, uint64_t host_bytes);
+NMX_API nmx_status_t nmx_safetensors_write(const char* path, int n, const char* const* names,
+                                           const char* const* dtypes, const int64_t* const* shapes, const int* ndims,
+                                           const void* const* data, int n_meta, const char* const* meta_keys,
+                                           const char* const* meta_values);
+/* Every tensor of an MLX checkpoint file the model has a slot for
+ * (nmx_model_load_tensor names; others are counted in n_skipped). With
+ * tp_size > 1, this rank's shard of q/k/v/gate/up rows and o/down K columns
+ * (the model must be the rank's local configuration). */
+NMX_API nmx_status_t nmx_model_load_safetensors(nmx_model_t model, const char* path, int tp_rank, int tp_size,
+                                                int* n_loaded, int* n_skipped);
+/* SSD prefix-block store, SSDCacheStore's file format
+ * (Sources/NovaMLXPrefixCache/SSDCacheStore.swift:132-135,194-269): the
+ * block's pages of every layer as tensors "i.0" (keys) and "i.1" (values),
+ * shape [1, kv heads, block tokens, head dim], in
+ * cache_dir/<first hex digit>/<hex of hash20>.safetensors with metadata
+ * block_hash, token_count, num_layers, model_name, created_at,
+ * layer_cache_types; load checks the layer count and the shapes. */
+NMX_API nmx_status_t nmx_ssd_save_block(nmx_kv_pool_t pool, int block_id, const uint8_t hash20[20], int token_count,
+                                        const char* model_name, const char* cache_dir);
+NMX_API nmx_status_t nmx_ssd_load_block(nmx_kv_pool_t pool, const uint8_t hash20[20], const char* cache_dir,
+                                        int block_id, int* token_count);
 
 /* ------------------------------------------------------------------------ */
 /* Tensor parallelism (one process per GPU). Each rank creates the model of

@@ -274,6 +274,18 @@ NMX_API nmx_status_t nmx_op_argmax(nmx_ctx_t ctx, const void* logits, int M, int
   return argmax_rows(&ctx->c, logits, M, V, dtype, out);
 }
 
+NMX_API nmx_status_t nmx_op_sample(nmx_ctx_t ctx, const void* logits, int M, int V, nmx_dtype_t dtype,
+                                   float temperature, float top_p, uint64_t seed, uint64_t counter, int32_t* out_ids,
+                                   float* out_logprob, int top_k, int32_t* out_top_ids, float* out_top_logprobs) {
+  API_BEGIN;
+  REQUIRE(ctx, "context");
+  if (M == 0) return NMX_OK;
+  REQUIRE(logits, "logits");
+  REQUIRE(out_ids, "out_ids");
+  return sample_rows(&ctx->c, logits, dtype, M, V, temperature, top_p, seed, counter, out_ids, out_logprob, top_k,
+                     out_top_ids, out_top_logprobs);
+}
+
 NMX_API nmx_status_t nmx_op_penalized_argmax(nmx_ctx_t ctx, const void* logits, int M, int V, nmx_dtype_t dtype,
                                              const int32_t* recent, const int32_t* n_recent, int max_recent,
                                              float penalty, int32_t* out) {

@@ -207,6 +207,10 @@ nmx_status_t rmsnorm(Ctx* c, const void* x, long ldx, const void* g, int M, int 
                      nmx_dtype_t dt, void* y, long ldy);
 nmx_status_t embed_rows(Ctx* c, const void* table, const int* ids, int T, int H, void* out);
 nmx_status_t argmax_rows(Ctx* c, const void* logits, int M, int V, nmx_dtype_t dt, int* out);
+// temperature / top-p categorical per row, chosen-id logprob, top_k logprobs (sampling.cu)
+nmx_status_t sample_rows(Ctx* c, const void* logits, nmx_dtype_t dt, int rows, int V, float temperature, float top_p,
+                         unsigned long long seed, unsigned long long counter, int* out_ids, float* out_lp, int top_k,
+                         int* top_ids, float* top_lp);
 nmx_status_t penalized_argmax(Ctx* c, const void* logits, int M, int V, nmx_dtype_t dt,
                               const int* recent, const int* n_recent, int max_recent,
                               float penalty, int* out);

@@ -157,6 +157,20 @@ _proto("nmx_spec_verify", _i, _vp, _vp, C.POINTER(SpecSeq), _i, _i, C.POINTER(C.
        C.POINTER(_i))
 VERIFY_NGRAM, VERIFY_PREFIX = 0, 1
 IPC_HANDLE_BYTES = 64
+_proto("nmx_op_sample", _i, _vp, _vp, _i, _i, _i, _f, _f, C.c_uint64, C.c_uint64, _vp, _vp, _i, _vp, _vp)
+_proto("nmx_safetensors_open", _i, C.c_char_p, C.POINTER(_vp))
+_proto("nmx_safetensors_close", None, _vp)
+_proto("nmx_safetensors_count", _i, _vp)
+_proto("nmx_safetensors_info", _i, _vp, _i, C.c_char_p, _i, C.c_char_p, C.POINTER(C.c_int64), C.POINTER(_i),
+       C.POINTER(C.c_uint64))
+_proto("nmx_safetensors_metadata", _i, _vp, C.c_char_p, C.c_char_p, _i)
+_proto("nmx_safetensors_read", _i, _vp, C.c_char_p, _vp, C.c_uint64)
+_proto("nmx_safetensors_write", _i, C.c_char_p, _i, C.POINTER(C.c_char_p), C.POINTER(C.c_char_p),
+       C.POINTER(C.POINTER(C.c_int64)), C.POINTER(_i), C.POINTER(_vp), _i, C.POINTER(C.c_char_p),
+       C.POINTER(C.c_char_p))
+_proto("nmx_model_load_safetensors", _i, _vp, C.c_char_p, _i, _i, C.POINTER(_i), C.POINTER(_i))
+_proto("nmx_ssd_save_block", _i, _vp, _i, C.c_char_p, _i, C.c_char_p, C.c_char_p)
+_proto("nmx_ssd_load_block", _i, _vp, C.c_char_p, C.c_char_p, _i, C.POINTER(_i))
 _proto("nmx_comm_create", _i, _vp, _i, _i, _sz, C.POINTER(_vp))
 _proto("nmx_comm_ipc_handle", _i, _vp, _vp)
 _proto("nmx_comm_connect", _i, _vp, _vp)
@@ -335,6 +349,21 @@ class Context:
         out = torch.empty((M,), dtype=torch.int32, device=logits.device)
         check(self._op(lambda: lib.nmx_op_argmax(self.h, _ptr(logits), M, V, _dt_of(logits), _ptr(out))))
         return out
+
+    def sample(self, logits, temperature: float, top_p: float = 1.0, seed: int = 0, counter: int = 0,
+               top_k: int = 0):
+        """temperature / top-p categorical per row; returns (ids, chosen logprobs,
+        top ids, top logprobs) as device tensors (the last two None when top_k == 0)"""
+        import torch
+        M, V = logits.shape
+        ids = torch.empty((M,), dtype=torch.int32, device=logits.device)
+        lp = torch.empty((M,), dtype=torch.float32, device=logits.device)
+        tid = torch.empty((M, max(top_k, 1)), dtype=torch.int32, device=logits.device)
+        tlp = torch.empty((M, max(top_k, 1)), dtype=torch.float32, device=logits.device)
+        check(self._op(lambda: lib.nmx_op_sample(self.h, _ptr(logits), M, V, _dt_of(logits), float(temperature),
+                                                 float(top_p), int(seed), int(counter), _ptr(ids), _ptr(lp),
+                                                 int(top_k), _ptr(tid), _ptr(tlp))))
+        return ids, lp, (tid if top_k else None), (tlp if top_k else None)
 
     def penalized_argmax(self, logits, recent, n_recent, penalty: float):
         import torch
@@ -955,3 +984,87 @@ def tp_shard(tensors: dict, cfg: ModelConfig, rank: int, world: int) -> dict:
         else:
             out[name] = t
     return out
+
+
+_ST_NP = {"U32": np.uint32, "F16": np.float16, "BF16": np.uint16, "F32": np.float32, "I32": np.int32,
+          "U8": np.uint8, "I64": np.int64, "U16": np.uint16}
+
+
+def safetensors_write(path: str, tensors: dict, metadata: Optional[dict] = None, dtypes: Optional[dict] = None):
+    """Write numpy arrays (name -> array) with an optional string metadata map.
+    dtypes overrides the stored dtype per name (e.g. "BF16" for raw uint16 bits)."""
+    names = list(tensors)
+    arrs = [np.ascontiguousarray(tensors[n]) for n in names]
+    rev = {np.dtype(np.uint32): "U32", np.dtype(np.float16): "F16", np.dtype(np.float32): "F32",
+           np.dtype(np.int32): "I32", np.dtype(np.uint8): "U8", np.dtype(np.int64): "I64",
+           np.dtype(np.uint16): "U16"}
+    dts = [(dtypes or {}).get(n) or rev[a.dtype] for n, a in zip(names, arrs)]
+    shapes = [(C.c_int64 * max(a.ndim, 1))(*a.shape) for a in arrs]
+    meta = metadata or {}
+    check(lib.nmx_safetensors_write(
+        path.encode(), len(names), (C.c_char_p * len(names))(*[n.encode() for n in names]),
+        (C.c_char_p * len(names))(*[d.encode() for d in dts]),
+        (C.POINTER(C.c_int64) * len(names))(*[C.cast(sh, C.POINTER(C.c_int64)) for sh in shapes]),
+        (_i * len(names))(*[a.ndim for a in arrs]), (_vp * len(names))(*[a.ctypes.data for a in arrs]),
+        len(meta), (C.c_char_p * len(meta))(*[k.encode() for k in meta]),
+        (C.c_char_p * len(meta))(*[str(v).encode() for v in meta.values()])))
+
+
+class SafetensorsFile:
+    """nmx_safetensors_t: read-only view of a .safetensors file."""
+
+    def __init__(self, path: str):
+        h = _vp()
+        check(lib.nmx_safetensors_open(path.encode(), C.byref(h)))
+        self.h = h
+
+    def tensors(self) -> dict:
+        out = {}
+        for i in range(lib.nmx_safetensors_count(self.h)):
+            name = C.create_string_buffer(1024)
+            dt = C.create_string_buffer(8)
+            shape = (C.c_int64 * 8)()
+            nd, nb = C.c_int(), C.c_uint64()
+            check(lib.nmx_safetensors_info(self.h, i, name, 1024, dt, shape, C.byref(nd), C.byref(nb)))
+            out[name.value.decode()] = (dt.value.decode(), tuple(shape[:nd.value]), nb.value)
+        return out
+
+    def read(self, name: str) -> np.ndarray:
+        dt, shape, nb = self.tensors()[name]
+        arr = np.empty(shape, dtype=_ST_NP[dt])
+        check(lib.nmx_safetensors_read(self.h, name.encode(), arr.ctypes.data, nb))
+        return arr
+
+    def metadata(self, key: str) -> Optional[str]:
+        n = lib.nmx_safetensors_metadata(self.h, key.encode(), None, 0)
+        if n < 0:
+            return None
+        buf = C.create_string_buffer(n + 1)
+        lib.nmx_safetensors_metadata(self.h, key.encode(), buf, n + 1)
+        return buf.value.decode()
+
+    def close(self):
+        if self.h:
+            lib.nmx_safetensors_close(self.h)
+            self.h = None
+
+    def __del__(self, _finalizing=sys.is_finalizing):
+        if not _finalizing():
+            self.close()
+
+
+def load_safetensors(model: "Model", path: str, tp_rank: int = 0, tp_size: int = 1):
+    """nmx_model_load_safetensors: returns (tensors loaded, tensors skipped)"""
+    n, k = C.c_int(), C.c_int()
+    check(lib.nmx_model_load_safetensors(model.h, path.encode(), tp_rank, tp_size, C.byref(n), C.byref(k)))
+    return n.value, k.value
+
+
+def ssd_save_block(pool: "KVPool", block_id: int, hash20: bytes, token_count: int, model_name: str, cache_dir: str):
+    check(lib.nmx_ssd_save_block(pool.h, block_id, hash20, token_count, model_name.encode(), cache_dir.encode()))
+
+
+def ssd_load_block(pool: "KVPool", hash20: bytes, cache_dir: str, block_id: int) -> int:
+    tc = C.c_int()
+    check(lib.nmx_ssd_load_block(pool.h, hash20, cache_dir.encode(), block_id, C.byref(tc)))
+    return tc.value
