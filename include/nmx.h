@@ -524,6 +524,11 @@ NMX_API nmx_status_t nmx_comm_connect(nmx_comm_t comm, const void* handles /* wo
 NMX_API void nmx_comm_destroy(nmx_comm_t comm);
 /* NULL detaches. Clears the model's captured decode graphs. */
 NMX_API nmx_status_t nmx_model_set_comm(nmx_model_t model, nmx_comm_t comm);
+/* 1: decode batches (9..128 rows) join the ranks' o_proj / down_proj
+ * partials inside the GEMM's epilogue, tile group by tile group; 0 (the
+ * default) runs the GEMM and the exchange kernel separately (same
+ * arithmetic, same bits). */
+NMX_API nmx_status_t nmx_model_set_exchange_fusion(nmx_model_t model, int enable);
 /* out[rows, cols] = res + sum over ranks of every rank's partial (f16, rank
  * order); every rank calls it with its own partial. */
 NMX_API nmx_status_t nmx_op_allreduce_resid(nmx_comm_t comm, const void* partial, int rows, int cols, const void* res,

@@ -29,6 +29,7 @@
 #include <cstring>
 #include <vector>
 
+#include "comm.h"
 #include "common.cuh"
 #include "kernels.h"
 #include "model.h"
@@ -37,7 +38,6 @@ namespace nmx {
 
 namespace {
 
-constexpr int kMaxRanks = 8;
 constexpr int kARThreads = 256;
 constexpr unsigned kARSpin = 1u << 24;
 
@@ -127,20 +127,25 @@ __global__ void __launch_bounds__(kARThreads) allreduce_resid_kernel(ARArgs a) {
 
 }  // namespace
 
-struct Comm {
-  Ctx* ctx = nullptr;
-  nmx_ctx_s* owner = nullptr;  // reference held on the context
-  int rank = 0, world = 1;
-  size_t region_bytes = 0;
-  unsigned char* arena = nullptr;          // this rank's arena
-  unsigned char* peer[kMaxRanks] = {};      // every rank's arena as mapped here
-  bool connected = false;
-  // arena layout
-  size_t off_r[2] = {0, 0}, off_flags = 0, off_epoch = 0, off_ticket = 0, bytes = 0;
-};
-
 size_t comm_region_bytes(const Comm* c) { return c->region_bytes; }
 void* comm_region(Comm* c, int r) { return c->arena + c->off_r[r]; }
+
+nmx_status_t comm_exchange_args(Comm* c, int region, ExchangeArgs* out) {
+  NMX_CHECK(c && c->connected, NMX_ERR_STATE, "exchange: communicator not connected");
+  ExchangeArgs x;
+  for (int q = 0; q < c->world; ++q) {
+    x.part[q] = reinterpret_cast<const half*>(c->peer[q] + c->off_r[region]);
+    x.peer_tflags[q] = reinterpret_cast<unsigned*>(c->peer[q] + c->off_tflags) + size_t(c->rank) * kMaxTileFlags;
+  }
+  x.my_tflags = reinterpret_cast<unsigned*>(c->arena + c->off_tflags);
+  x.epoch = reinterpret_cast<unsigned*>(c->arena + c->off_epoch);
+  x.ticket = reinterpret_cast<unsigned*>(c->arena + c->off_tticket);
+  x.part_local = reinterpret_cast<half*>(c->arena + c->off_r[region]);
+  x.world = c->world;
+  x.rank = c->rank;
+  *out = x;
+  return NMX_OK;
+}
 
 nmx_status_t comm_allreduce_resid(Comm* cm, int region, int rows, int cols, const void* res, long ldres, void* out,
                                   long ldo, unsigned* err) {
@@ -204,7 +209,9 @@ NMX_API nmx_status_t nmx_comm_create(nmx_ctx_t ctx, int rank, int world, size_t 
   c.off_flags = 2 * c.region_bytes;
   c.off_epoch = c.off_flags + 256;
   c.off_ticket = c.off_epoch + 256;
-  c.bytes = c.off_ticket + 256;
+  c.off_tflags = c.off_ticket + 256;
+  c.off_tticket = c.off_tflags + size_t(nmx::kMaxRanks) * nmx::kMaxTileFlags * 4;
+  c.bytes = c.off_tticket + 256;
   cudaError_t e = cudaSetDevice(c.ctx->device);
   if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&c.arena), c.bytes);
   if (e == cudaSuccess) e = cudaMemset(c.arena, 0, c.bytes);
@@ -300,6 +307,14 @@ NMX_API nmx_status_t nmx_model_set_comm(nmx_model_t model, nmx_comm_t comm) {
   m->comm = &c;
   m->comm_handle = comm;
   m->graphs_clear();  // captured steps have no exchange
+  return NMX_OK;
+}
+
+NMX_API nmx_status_t nmx_model_set_exchange_fusion(nmx_model_t model, int enable) {
+  nmx::clear_error();
+  NMX_CHECK(model != nullptr, NMX_ERR_INVALID, "nmx_model_set_exchange_fusion: null model");
+  model->m->fused_exchange = enable != 0;
+  model->m->graphs_clear();
   return NMX_OK;
 }
 

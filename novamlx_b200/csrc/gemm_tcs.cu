@@ -38,6 +38,7 @@
 #include <map>
 #include <mutex>
 
+#include "comm.h"
 #include "common.cuh"
 #include "kernels.h"
 #include "tc_common.cuh"
@@ -87,6 +88,10 @@ struct TcsArgs {
   unsigned* counters;      // [groups], zero between launches
   unsigned* err;
   bool weights_static;
+  // tensor parallelism (residual epilogue only): this rank's partial goes
+  // to its exchange region and the CTA sums every rank's (fused exchange)
+  bool fused;
+  ExchangeArgs x;
 };
 
 // 16-row record tile r8 (0..7) of weight tile `at`
@@ -115,6 +120,48 @@ __device__ __forceinline__ half epi_value(const TcsArgs& a, float acc, float up,
 }
 
 __device__ __forceinline__ void dq_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kSDW * 32) : "memory"); }
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+constexpr unsigned kXSpin = 1u << 24;
+
+// Fused exchange: this CTA's partial rows are in its region; publish slot
+// `slot` at epoch e to every rank and wait (bounded) until every rank has
+// published it. Called by all epilogue threads.
+__device__ __forceinline__ bool tp_exchange(const ExchangeArgs& x, int slot, unsigned e, unsigned* err, int* s_ok) {
+  __threadfence_system();
+  dq_bar();
+  if (threadIdx.x == 0) {
+    for (int q = 0; q < x.world; ++q) st_release_sys(x.peer_tflags[q] + slot, e);
+    int ok = 1;
+    for (int q = 0; q < x.world && ok; ++q) {
+      unsigned it = 0;
+      while ((int)(ld_acquire_sys(x.my_tflags + size_t(q) * kMaxTileFlags + slot) - e) < 0)
+        if (++it >= kXSpin) {
+          ok = 0;
+          atomicOr(err, 1u);
+          break;
+        }
+    }
+    *s_ok = ok;
+  }
+  dq_bar();
+  return *s_ok != 0;
+}
+
+// y = res + Σ_ranks partial (f16 partials summed in rank order in f32, then
+// rounded) — the rule of the separate exchange kernel
+__device__ __forceinline__ half tp_combine(const ExchangeArgs& x, const half* res, long ldres, long ld, int m, long n) {
+  float acc = 0.f;
+  for (int q = 0; q < x.world; ++q) acc += __half2float(__ldcg(x.part[q] + (long)m * ld + n));
+  return __float2half_rn(__half2float(res[(long)m * ldres + n]) + rnd<half>(acc));
+}
 
 // Weight row (record r8 of the tile, row g16 of the record) held by TMEM
 // lane L. The eight lanes of each quarter warp take rows g, g+1 (g even) of
@@ -196,6 +243,8 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
   __shared__ uint32_t s_taddr;
   __shared__ int s_fail;
   __shared__ unsigned s_last;  // every share of the group has stored its partials
+  __shared__ unsigned s_epoch;  // fused exchange: this launch's epoch
+  __shared__ int s_xok;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int grp = blockIdx.x, share = blockIdx.y;
@@ -398,6 +447,11 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
     const int trow = er8 * 16 + eg16;    // and the weight row of the tile it holds
     const uint32_t lane_addr = taddr + (uint32_t(32 * quad) << 16);
     const bool ok = !s_fail;
+    const bool fused = EPI == EPI_RESID && a.fused;
+    if (fused) {
+      if (tid == 0) s_epoch = *reinterpret_cast<volatile unsigned*>(a.x.epoch) + 1u;
+      dq_bar();
+    }
     if (a.S == 1) {
       constexpr int STEP = EPI == EPI_SILU ? 2 : 1;
       for (int ti = 0; ti < ntl; ti += STEP) {
@@ -410,9 +464,23 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
               const int m = c0 + j;
-              if (m < a.M) a.y[(long)m * a.ldy + n] = epi_value<EPI>(a, v[j], EPI == EPI_SILU ? u[j] : 0.f, m, n);
+              if (m >= a.M) continue;
+              if (fused)
+                a.x.part_local[(long)m * a.ldy + n] = __float2half_rn(v[j]);
+              else
+                a.y[(long)m * a.ldy + n] = epi_value<EPI>(a, v[j], EPI == EPI_SILU ? u[j] : 0.f, m, n);
             }
           }
+        }
+      }
+      if (fused && tp_exchange(a.x, grp, s_epoch, a.err, &s_xok) && ok) {
+        for (int ti = 0; ti < ntl; ++ti) {
+          const long n = (long)(t0 + ti) * 128 + trow;
+          for (int c0 = 8 * part; c0 < NT; c0 += 8 * kDG)
+            for (int j = 0; j < 8; ++j) {
+              const int m = c0 + j;
+              if (m < a.M) a.y[(long)m * a.ldy + n] = tp_combine(a.x, a.res, a.ldres, a.ldy, m, n);
+            }
         }
       }
     } else {
@@ -473,13 +541,36 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
             int pr8, pg16;
             lane_row(4 * r4 + q, pr8, pg16);
             const long n = n0 + pr8 * 16 + pg16;
-            a.y[(long)m * a.ldy + n] = epi_value<EPI>(a, av[q], uv[q], m, n);
+            if (fused)
+              a.x.part_local[(long)m * a.ldy + n] = __float2half_rn(av[q]);
+            else
+              a.y[(long)m * a.ldy + n] = epi_value<EPI>(a, av[q], uv[q], m, n);
+          }
+        }
+      }
+      if (fused && tp_exchange(a.x, grp * a.S + share, s_epoch, a.err, &s_xok) && ok && all_in) {
+        for (int e = e_lo + tid; e < e_hi; e += kSDW * 32) {
+          const int r4 = e & 31, m = (e >> 5) % a.M, ti = (e >> 5) / a.M;
+          const long n0 = (long)(t0 + ti) * 128;
+          for (int q = 0; q < 4; ++q) {
+            int pr8, pg16;
+            lane_row(4 * r4 + q, pr8, pg16);
+            const long n = n0 + pr8 * 16 + pg16;
+            a.y[(long)m * a.ldy + n] = tp_combine(a.x, a.res, a.ldres, a.ldy, m, n);
           }
         }
       }
       // the second round of arrivals: the last share resets the counter
       dq_bar();
       if (tid == 0 && atomicAdd(a.counters + grp, 1u) == unsigned(2 * a.S - 1)) a.counters[grp] = 0u;
+    }
+    if (fused && tid == 0) {
+      // the last CTA records the epoch for the next exchange
+      __threadfence();
+      if (atomicAdd(a.x.ticket, 1u) == gridDim.x * gridDim.y - 1u) {
+        *a.x.ticket = 0u;
+        *a.x.epoch = s_epoch;
+      }
     }
   }
 
@@ -609,6 +700,13 @@ nmx_status_t qgemm_tcs(Ctx* c, const GemvDLArgs& a, int epi) {
   g.counters = a.counters;
   g.err = a.err;
   g.weights_static = a.weights_static;
+  g.fused = false;
+  if (a.comm) {
+    NMX_CHECK(epi == EPI_RESID && a.res != nullptr, NMX_ERR_INVALID, "qgemm_tcs: the exchange needs the residual epilogue");
+    NMX_CHECK(long(p.groups) * p.S <= kMaxTileFlags, NMX_ERR_UNSUPPORTED, "qgemm_tcs: too many exchange slots");
+    NMX_TRY(comm_exchange_args(static_cast<Comm*>(a.comm), a.comm_region, &g.x));
+    g.fused = true;
+  }
   switch (epi) {
     case EPI_STORE: return launch_tcs<EPI_STORE>(c, tm, tw, g, p);
     case EPI_RESID: return launch_tcs<EPI_RESID>(c, tm, tw, g, p);

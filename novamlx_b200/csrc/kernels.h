@@ -75,6 +75,11 @@ struct GemvDLArgs {
   // programmatic-launch wait
   bool weights_static = false;
   unsigned* err = nullptr;            // device word: bit 0 = a bounded wait ran out
+  // tensor parallelism (qgemm_tcs, residual epilogue): the communicator
+  // (Comm*) and partial region whose exchange the GEMM fuses; y = res +
+  // sum over ranks of x · W_rankᵀ
+  void* comm = nullptr;
+  int comm_region = 0;
 };
 bool qgemv_dl_supported(int bits, int gs, nmx_dtype_t dt, int N, int K);
 int qgemv_dl_max_m(int K, int epi);
@@ -187,6 +192,12 @@ nmx_status_t persist_launch(Ctx* c, const PersistArgs& A, size_t smem);
 // fused = 1: apply RoPE to q and append the row's own k/v (one query row per
 // sequence, decode); fused = 0: q is already roped and K/V already appended.
 nmx_status_t paged_attention(Ctx* c, const AttnArgs& a, bool fused);
+// prefill chunks / mixed batches: query blocks of up to 16 rows of one
+// sequence (attention_prefill.cu). prefill_items cuts the batch's rows
+// (row_seq: sequence of each row, rows of a sequence consecutive) into
+// items (first row, rows); at most T items.
+int prefill_items(const int32_t* row_seq, int T, int2* items_host);
+nmx_status_t paged_prefill_attention(Ctx* c, const AttnArgs& a, const int2* items, int n_items);
 // the tensor-core implementation behind paged_attention (attention_mma.cu)
 nmx_status_t paged_attention_mma(Ctx* c, const AttnArgs& a, bool fused);
 

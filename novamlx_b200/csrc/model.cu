@@ -190,6 +190,7 @@ nmx_status_t Model::create(Ctx* c, const nmx_model_cfg& cfg, Model** out) {
       {reinterpret_cast<void**>(&m->tok_seq), size_t(T) * 4},
       {reinterpret_cast<void**>(&m->tok_pos), size_t(T) * 4},
       {reinterpret_cast<void**>(&m->last_rows), size_t(rows_logits) * 4},
+      {reinterpret_cast<void**>(&m->pf_items), size_t(T) * 8},
       {reinterpret_cast<void**>(&m->out_ids), size_t(rows_logits) * 4},
       {reinterpret_cast<void**>(&m->block_tables), size_t(B) * kBlockCap * 4},
       {reinterpret_cast<void**>(&m->hist), size_t(kHistCap) * 4},
@@ -247,7 +248,7 @@ nmx_status_t Model::create(Ctx* c, const nmx_model_cfg& cfg, Model** out) {
     e = cudaMemcpyAsync(m->inv_freq, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice, c->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
   // pinned staging for per-call step descriptors
-  m->pinned_bytes = size_t(T) * 3 * 4 + size_t(B) * kBlockCap * 4 + size_t(rows_logits) * 4 + 4096;
+  m->pinned_bytes = size_t(T) * 3 * 4 + size_t(B) * kBlockCap * 4 + size_t(rows_logits) * 4 + size_t(T) * 8 + 4096;
   if (e == cudaSuccess) e = cudaMallocHost(reinterpret_cast<void**>(&m->pinned), m->pinned_bytes);
   if (e != cudaSuccess) {
     set_error(std::string("model workspace: ") + cudaGetErrorString(e));
@@ -561,6 +562,19 @@ nmx_status_t Model::linear(const Lin& l, const void* x, long ldx, const void* ga
 nmx_status_t Model::block_out(const Lin& l, const void* x, long ldx, int M, int region) {
   const int H = cfg.hidden;
   if (!comm) return linear(l, x, ldx, nullptr, M, H, 0, nullptr, h, H, h, H, EPI_RESID);
+  if (fused_exchange && l.dl && M >= kTcsMinRows && M <= kTcsMaxRows && qgemm_tcs_supported(M, H, l.K, EPI_RESID)) {
+    // one kernel: the decode-batch GEMM joins the ranks' partials in its
+    // epilogue, tile group by tile group, over peer memory
+    GemvDLArgs a;
+    a.x = x; a.ldx = ldx; a.w = l.w; a.N = H; a.K = l.K; a.M = M;
+    a.y = h; a.ldy = H; a.res = h; a.ldres = H;
+    a.partials = dl_partials; a.partials_cap = dl_partials_cap; a.counters = dl_counters;
+    a.weights_static = true;
+    a.err = ctx->dev_err;
+    a.comm = comm;
+    a.comm_region = region;
+    return qgemm_tcs(ctx, a, EPI_RESID);
+  }
   NMX_TRY(linear(l, x, ldx, nullptr, M, H, 0, nullptr, comm_region(comm, region), H, nullptr, 0, EPI_STORE));
   return comm_allreduce_resid(comm, region, M, H, h, H, h, H, ctx->dev_err);
 }
@@ -615,7 +629,7 @@ nmx_status_t Model::run_layers_prefill(KvPool* pool, int T) {
     at.counters = attn_counters;
     at.T = T; at.Hq = cf.n_heads; at.Hkv = cf.n_kv_heads; at.D = cf.head_dim; at.BT = kBT;
     at.splits = 1; at.scale = 1.0f / std::sqrt(float(cf.head_dim));
-    NMX_TRY(paged_attention(c, at, false));
+    NMX_TRY(paged_prefill_attention(c, at, pf_items, n_pf_items));
 
     NMX_TRY(block_out(ly.o, attn, Nq, T, 0));
 
@@ -749,6 +763,13 @@ nmx_status_t Model::upload_batch(const nmx_seq_t* seqs, int n, int* T_out, bool*
   NMX_CUDA_OK(cudaMemcpy2DAsync(block_tables, size_t(kBlockCap) * 4, tbl, size_t(kBlockCap) * 4, size_t(nb_max) * 4,
                                 size_t(n), cudaMemcpyHostToDevice, c->stream));
   h2d_bytes_last = size_t(T) * 12 + size_t(n) * 4 + size_t(n) * nb_max * 4;
+  n_pf_items = 0;
+  if (!decode) {
+    int2* items = reinterpret_cast<int2*>(tbl + size_t(max_batch) * kBlockCap);
+    n_pf_items = prefill_items(sq, T, items);
+    NMX_CUDA_OK(cudaMemcpyAsync(pf_items, items, size_t(n_pf_items) * 8, cudaMemcpyHostToDevice, c->stream));
+    h2d_bytes_last += size_t(n_pf_items) * 8;
+  }
   *T_out = T;
   *decode_out = decode;
   return NMX_OK;

@@ -65,6 +65,8 @@ struct Model {
   int* am_idx = nullptr;
   unsigned* am_counter = nullptr;
   int *tok_ids = nullptr, *tok_seq = nullptr, *tok_pos = nullptr, *last_rows = nullptr, *out_ids = nullptr;
+  int2* pf_items = nullptr;  // prefill attention work items of the current batch
+  int n_pf_items = 0;
   int *block_tables = nullptr, *hist = nullptr, *step = nullptr;
   float* inv_freq = nullptr;
   char* pinned = nullptr;
@@ -118,6 +120,7 @@ struct Model {
   // are exchanged and summed (with the residual) through the communicator
   Comm* comm = nullptr;
   nmx_comm_s* comm_handle = nullptr;
+  bool fused_exchange = false;  // decode batches: the GEMM epilogue does the exchange (nmx_model_set_exchange_fusion)
   bool persistent_enabled = false;  // opt-in: the per-layer graph is faster today
   bool persistent_unusable = false;  // the device refused the launch (cooperative / shared memory)
   PPhase* pers_ph = nullptr;

@@ -286,7 +286,7 @@ def spec(ctx, torch, nmx, batch, ctx_len, n_drafts, cycles, layers, draft_layers
             "target_weight_bytes": target.step_weight_bytes, "draft_weight_bytes": draft.step_weight_bytes}
 
 
-def tp(torch, nmx, batch, ctx_len, steps, layers, prefill):
+def tp(torch, nmx, batch, ctx_len, steps, layers, prefill, fuse=True):
     import numpy as np
     import os
     import torch.distributed as dist
@@ -304,6 +304,7 @@ def tp(torch, nmx, batch, ctx_len, steps, layers, prefill):
     if world > 1:
         comm = nmx.tp_comm(ctx, rank, world, max_tokens * cfg.hidden * 2, nmx.torch_exchange(dist))
         m.set_comm(comm)
+        m.set_exchange_fusion(fuse)
     nblk = (ctx_len + steps + 64 + 15) // 16
     pblk = ((prefill or 0) + 15) // 16
     pool = nmx.KVPool(m, batch * nblk + pblk + 2)
@@ -328,6 +329,7 @@ def tp(torch, nmx, batch, ctx_len, steps, layers, prefill):
     m.decode_greedy(pool, first, [ctx_len] * batch, tables, 4, want_ids=False)  # graphs, attributes
     ms = timed(lambda: m.decode_greedy(pool, first, [ctx_len] * batch, tables, steps, want_ids=False))
     out = {"what": "tensor-parallel decode", "model": "qwen2.5-32b-style", "layers": layers, "tp": world,
+           "exchange": "fused into the GEMM" if fuse else "separate kernel",
            "batch": batch, "ctx": ctx_len, "steps": steps, "ms_per_step": round(ms / steps, 3),
            "tok_s": round(batch * steps * 1000.0 / ms, 1),
            "weight_bytes_per_rank": m.step_weight_bytes, "kv_bytes_per_token_per_rank": m.kv_bytes_per_token}
@@ -370,6 +372,7 @@ def main():
     ap.add_argument("--oracle-draft", action="store_true")
     ap.add_argument("--steps", type=int, default=16)
     ap.add_argument("--prefill", type=int, default=0)
+    ap.add_argument("--no-fuse", action="store_true", help="tp: GEMM and exchange as separate kernels")
     a = ap.parse_args()
     if a.copies is None:
         a.copies = 1 if a.what == "gemm" else 3
@@ -383,7 +386,7 @@ def main():
         a.m = 2048 if a.what == "gemm" else 1
     if a.what == "tp":
         r = tp(torch, nmx, a.batch if a.batch != 1 else 32, a.ctx if a.ctx != 2048 else 8192, a.steps, a.layers,
-               a.prefill)
+               a.prefill, not a.no_fuse)
         if r is not None:
             print(json.dumps(r), flush=True)
         return

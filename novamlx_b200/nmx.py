@@ -177,6 +177,7 @@ _proto("nmx_comm_connect", _i, _vp, _vp)
 _proto("nmx_comm_destroy", None, _vp)
 _proto("nmx_model_set_comm", _i, _vp, _vp)
 _proto("nmx_op_allreduce_resid", _i, _vp, _vp, _i, _i, _vp, _vp)
+_proto("nmx_model_set_exchange_fusion", _i, _vp, _i)
 _proto("nmx_block_pool_destroy", None, _vp)
 _proto("nmx_block_pool_allocate", _i, _vp)
 _proto("nmx_block_pool_free", None, _vp, _i)
@@ -530,6 +531,9 @@ class Model:
         """tensor parallelism: join o_proj / down_proj outputs over the ranks"""
         check(lib.nmx_model_set_comm(self.h, comm.h if comm is not None else None))
         self.comm = comm  # keep it alive while the model uses it
+
+    def set_exchange_fusion(self, enable: bool):
+        check(lib.nmx_model_set_exchange_fusion(self.h, int(bool(enable))))
 
     def load_tensor(self, name: str, arr: np.ndarray):
         arr = np.ascontiguousarray(arr)

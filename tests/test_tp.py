@@ -103,3 +103,10 @@ def test_tp2_matches_unsharded(nmx, tmp_path, name):
     assert np.array_equal(r0["tp_first"], r0["full_first"])
     agree = float(np.mean(r0["tp_ids"] == r0["full_ids"]))
     assert agree >= 0.9, agree
+    # decode-batch GEMM with the exchange in its epilogue: the same bits as
+    # GEMM + exchange kernel, the same bits on both ranks, close to unsharded
+    assert np.array_equal(r0["tp_batch"], r0["tp_batch_sep"])
+    assert np.array_equal(r0["tp_batch"], r1["tp_batch"])
+    for g, f in zip(r0["tp_batch"], r0["full_batch"]):
+        assert O.cosine(g, f) >= 0.999
+        assert O.max_rel_err(g, f) <= 2e-2

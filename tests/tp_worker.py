@@ -33,6 +33,20 @@ def run(nmx, m, pool, rng_seed, cfg):
     return logits, first, ids
 
 
+def run_batch(nmx, m, pool, rng_seed, cfg):
+    """12 short prompts prefilled together (96 rows) and one 12-row decode
+    step: the decode-batch GEMM path, whose epilogue can do the exchange"""
+    rng = np.random.default_rng(rng_seed)
+    prompts = [rng.integers(0, cfg.vocab, 8) for _ in range(12)]
+    tables = [np.array([100 + i], np.int32) for i in range(12)]
+    pre = m.forward(pool, [dict(tokens=p, start_pos=0, block_table=t) for p, t in zip(prompts, tables)],
+                    nmx.OUT_LOGITS_LAST)
+    toks = rng.integers(0, cfg.vocab, 12)
+    dec = m.forward(pool, [dict(tokens=[int(x)], start_pos=8, block_table=t) for x, t in zip(toks, tables)],
+                    nmx.OUT_LOGITS_LAST)
+    return np.concatenate([pre, dec])
+
+
 def main():
     import torch
     import torch.distributed as dist
@@ -56,7 +70,7 @@ def main():
         m.load_tensor(k, v.view(np.float16) if v.dtype == np.uint16 else v)
     comm = nmx.tp_comm(ctx, rank, world, full_cfg.max_tokens * full_cfg.hidden * 2, nmx.torch_exchange(dist))
     m.set_comm(comm)
-    pool = nmx.KVPool(m, 40)
+    pool = nmx.KVPool(m, 120)
 
     # op-level exchange: rank r contributes (r + 1) * base
     base = torch.arange(64 * 512, device=f"cuda:{rank}", dtype=torch.float32).reshape(64, 512) % 7 - 3
@@ -70,17 +84,23 @@ def main():
     op_ok = bool(torch.equal(out, expect))
 
     tp_logits, tp_first, tp_ids = run(nmx, m, pool, 11, full_cfg)
+    m.set_exchange_fusion(True)
+    tp_batch = run_batch(nmx, m, pool, 12, full_cfg)       # exchange fused into the GEMM
+    m.set_exchange_fusion(False)
+    tp_batch_sep = run_batch(nmx, m, pool, 12, full_cfg)   # GEMM, then the exchange kernel
     dist.barrier()
     m.set_comm(None)
     comm.close()
-    result = dict(op_ok=np.array(op_ok), tp_logits=tp_logits, tp_first=tp_first, tp_ids=tp_ids)
+    result = dict(op_ok=np.array(op_ok), tp_logits=tp_logits, tp_first=tp_first, tp_ids=tp_ids,
+                  tp_batch=tp_batch, tp_batch_sep=tp_batch_sep)
     if rank == 0:
         fm = nmx.Model(ctx, full_cfg)
         for k, v in tensors.items():
             fm.load_tensor(k, v.view(np.float16) if v.dtype == np.uint16 else v)
-        fpool = nmx.KVPool(fm, 40)
+        fpool = nmx.KVPool(fm, 120)
         f_logits, f_first, f_ids = run(nmx, fm, fpool, 11, full_cfg)
-        result.update(full_logits=f_logits, full_first=f_first, full_ids=f_ids)
+        f_batch = run_batch(nmx, fm, fpool, 12, full_cfg)
+        result.update(full_logits=f_logits, full_first=f_first, full_ids=f_ids, full_batch=f_batch)
     np.savez(f"{a.out}.rank{rank}.npz", **result)
     dist.barrier()
     dist.destroy_process_group()
