@@ -204,8 +204,29 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
         break;
       }
       const unsigned char* rawb = raw + rs * kRawBytes;
-      // thread t fills weight row t of the tile: record t / 16, row t % 16
-      tc::dequant_record_row(rawb + (tid >> 4) * tc::kRecPad, tid & 15, gi, B, tid);
+      // warp w fills record halves 4w .. 4w+3 (8 tile rows each): lane 4g+t
+      // reads its 16 bytes of the half (words 2t, 2t+1 of both groups of row
+      // g: one conflict-free 512-byte sweep per warp) and writes chunks 2t,
+      // 2t+1 of tile row 8·(half index) + g (conflict-free in the swizzle)
+      {
+        const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int hh = warp * 4 + j;  // record hh / 2, rows 8·(hh % 2) ..
+          const unsigned char* rec = rawb + (hh >> 1) * tc::kRecPad;
+          const int hf = hh & 1;
+          const uint4 wv = *reinterpret_cast<const uint4*>(rec + hf * 512 + 16 * lane);
+          const __half sc = *reinterpret_cast<const __half*>(rec + 1024 + ((0 * 2 + gi) * 8 + g) * 4 + hf * 2);
+          const __half bi = *reinterpret_cast<const __half*>(rec + 1024 + ((1 * 2 + gi) * 8 + g) * 4 + hf * 2);
+          const __half2 s2 = __halves2half2(sc, sc);
+          const __half2 s16 = __hmul2(s2, __float2half2_rn(0.0625f));
+          const __half2 b2 = __halves2half2(bi, bi);
+          const int row = hh * 8 + g;
+          const uint32_t w0 = gi ? wv.z : wv.x, w1 = gi ? wv.w : wv.y;
+          *reinterpret_cast<uint4*>(B + tc::sw128(row, 2 * t)) = tc::dequant_word_chunk(w0, s2, s16, b2);
+          *reinterpret_cast<uint4*>(B + tc::sw128(row, 2 * t + 1)) = tc::dequant_word_chunk(w1, s2, s16, b2);
+        }
+      }
       // generic-proxy writes, read by the tensor core's async proxy
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_arrive(&full[s]);

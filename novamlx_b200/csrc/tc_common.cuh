@@ -98,6 +98,26 @@ __device__ __forceinline__ int sw128(int row, int chunk) {
   return (row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4);
 }
 
+// one 32-bit word (8 nibbles, k 8w .. 8w+7 of a group) as 8 f16 weights
+// w = s·q + b in k order (one 16-byte chunk of a K-major tile row)
+__device__ __forceinline__ uint4 dequant_word_chunk(uint32_t word, __half2 s2, __half2 s16, __half2 b2) {
+  const __half2 k1024 = __float2half2_rn(1024.f);
+  uint32_t P[4];
+  dequant_word<4>(word, P);  // (q0,q4), (16q1,16q5), (q2,q6), (16q3,16q7), each + 1024
+  __half2 v0 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&P[0]), k1024), s2, b2);   // w0, w4
+  __half2 v1 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&P[1]), k1024), s16, b2);  // w1, w5
+  __half2 v2 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&P[2]), k1024), s2, b2);   // w2, w6
+  __half2 v3 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&P[3]), k1024), s16, b2);  // w3, w7
+  const uint32_t u0 = *reinterpret_cast<uint32_t*>(&v0), u1 = *reinterpret_cast<uint32_t*>(&v1);
+  const uint32_t u2 = *reinterpret_cast<uint32_t*>(&v2), u3 = *reinterpret_cast<uint32_t*>(&v3);
+  uint4 o;
+  o.x = __byte_perm(u0, u1, 0x5410);  // w0, w1
+  o.y = __byte_perm(u2, u3, 0x5410);  // w2, w3
+  o.z = __byte_perm(u0, u1, 0x7632);  // w4, w5
+  o.w = __byte_perm(u2, u3, 0x7632);  // w6, w7
+  return o;
+}
+
 // Row g16 (0..15) of one decode record, group gi (k 0-63 or 64-127), as 64
 // f16 weights w = s·q + b (rounded to f16) into row `row` of a swizzled
 // 64-wide tile. Record layout: bytes [0, 512) rows 0-7, [512, 1024) rows
