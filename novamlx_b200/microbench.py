@@ -286,7 +286,7 @@ def spec(ctx, torch, nmx, batch, ctx_len, n_drafts, cycles, layers, draft_layers
             "target_weight_bytes": target.step_weight_bytes, "draft_weight_bytes": draft.step_weight_bytes}
 
 
-def tp(torch, nmx, batch, ctx_len, steps, layers, prefill, fuse=True):
+def tp(torch, nmx, batch, ctx_len, steps, layers, prefill, fuse=False):
     import numpy as np
     import os
     import torch.distributed as dist
@@ -372,7 +372,7 @@ def main():
     ap.add_argument("--oracle-draft", action="store_true")
     ap.add_argument("--steps", type=int, default=16)
     ap.add_argument("--prefill", type=int, default=0)
-    ap.add_argument("--no-fuse", action="store_true", help="tp: GEMM and exchange as separate kernels")
+    ap.add_argument("--fuse", action="store_true", help="tp: exchange fused into the decode-batch GEMM epilogue")
     a = ap.parse_args()
     if a.copies is None:
         a.copies = 1 if a.what == "gemm" else 3
@@ -386,7 +386,7 @@ def main():
         a.m = 2048 if a.what == "gemm" else 1
     if a.what == "tp":
         r = tp(torch, nmx, a.batch if a.batch != 1 else 32, a.ctx if a.ctx != 2048 else 8192, a.steps, a.layers,
-               a.prefill, not a.no_fuse)
+               a.prefill, a.fuse)
         if r is not None:
             print(json.dumps(r), flush=True)
         return

@@ -61,7 +61,7 @@ def main():
     dist.init_process_group("gloo", init_method="env://")
     torch.cuda.set_device(rank)
     d = tiny(a.model)
-    full_cfg = nmx.ModelConfig(**d, max_batch=8, max_tokens=256)
+    full_cfg = nmx.ModelConfig(**d, max_batch=16, max_tokens=256)
     tensors = O.random_tensors(O.TinyCfg(**d), seed=5, std=0.05)
     shard = nmx.tp_shard(tensors, full_cfg, rank, world)
     ctx = nmx.Context(rank)
