@@ -9,10 +9,12 @@
 // softmax in the log2 domain on the accumulator fragments, and O += P·V with
 // P taken straight from the S fragments and V fed by ldmatrix.trans. The
 // warps' states merge through shared memory. The splits of one (row, kv
-// head) run as one thread-block cluster (<= 16 CTAs): after a cluster
-// barrier each CTA reads the others' (max, denominator) and numerators
-// through distributed shared memory and writes its slice of the outputs; no
-// global scratch, atomics or fences.
+// head) run as one thread-block cluster (<= 16 CTAs): each CTA stores its
+// (max, denominator) pairs into every CTA of the cluster and each of its
+// numerators into the CTA that owns that output element (remote shared
+// memory stores, which do not wait for an answer), then after one cluster
+// barrier each CTA combines its slice of the outputs from its own shared
+// memory; no global scratch, atomics or fences.
 //
 // In decode (FUSED) the CTA also applies RoPE to q; the split holding the new
 // position writes the new token's roped k and its v to the page (for later
@@ -41,20 +43,23 @@ __device__ __forceinline__ unsigned cluster_rank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-// all threads of all CTAs of the cluster; orders shared-memory writes before
-// the barrier against reads of them (also remote ones) after it
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+// the two halves of a cluster barrier: arrive (relaxed: the start of the
+// kernel, to mark that this CTA runs; release: after the remote stores) and
+// wait (acquire)
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
-// a float in the shared memory of CTA `rank` of the cluster, at the address
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// stores v to the shared memory of CTA `rank` of the cluster, at the address
 // `p` has in this CTA
-__device__ __forceinline__ float ld_dsmem(const void* p, unsigned rank) {
+__device__ __forceinline__ void st_dsmem(void* p, unsigned rank, float v) {
   const unsigned la = static_cast<unsigned>(__cvta_generic_to_shared(p));
   unsigned ra;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(la), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
-  return v;
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
 }
 
 template <int D, bool FUSED>
@@ -71,7 +76,10 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
   // per-warp softmax states; entry kAW is the new token (FUSED, owner split)
   __shared__ float s_m[kAW + 1][kMaxRepA], s_l[kAW + 1][kMaxRepA];
   __shared__ float c_ml[kMaxRepA][2];  // this split's (max, denominator) per q head
+  // every split's (max, denominator) per q head, stored here by the splits
   __shared__ float s_cm[kMaxRepA][kMaxClusterA], s_cl[kMaxRepA][kMaxClusterA];
+  // numerators of this CTA's output slice, one row of slot_len per split
+  __shared__ float s_rnum[kMaxRepA * D + kMaxClusterA];
   __shared__ float s_w[kMaxRepA][kMaxClusterA];
   __shared__ __align__(16) half s_knew[D];
   __shared__ __align__(16) half s_vnew[D];
@@ -80,6 +88,9 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   const int Hq = a.Hq, Hkv = a.Hkv, rep = Hq / Hkv, S = gridDim.x;
+  // phase 1 of the cluster barrier: this CTA runs (its shared memory may be
+  // written by the others once the phase completes)
+  if (S > 1) cluster_arrive_relaxed();
   half* Kc = reinterpret_cast<half*>(a.k_cache);
   half* Vc = reinterpret_cast<half*>(a.v_cache);
 
@@ -317,15 +328,22 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
   }
   if (S == 1) return;
 
-  // ---- split-KV: the splits of (row, h) are one cluster; each CTA combines
-  // a slice of the outputs from the others' shared memory
-  cluster_sync();
+  // ---- split-KV: the splits of (row, h) are one cluster. Output element e
+  // of the rep * D belongs to split o with o E / S <= e < (o + 1) E / S.
+  const int E = rep * D, slot_len = (E + S - 1) / S;
+  __syncthreads();
+  cluster_wait();  // phase 1: every CTA of the cluster runs
+  for (int e = tid; e < E; e += kAW * 32) {
+    const int o = ((e + 1) * S - 1) / E;
+    st_dsmem(&s_rnum[split * slot_len + e - o * E / S], unsigned(o), c_num[e]);
+  }
   if (tid < rep * S) {
     const int hi = tid / S, s2 = tid % S;
-    s_cm[hi][s2] = ld_dsmem(&c_ml[hi][0], unsigned(s2));
-    s_cl[hi][s2] = ld_dsmem(&c_ml[hi][1], unsigned(s2));
+    st_dsmem(&s_cm[hi][split], unsigned(s2), c_ml[hi][0]);
+    st_dsmem(&s_cl[hi][split], unsigned(s2), c_ml[hi][1]);
   }
-  __syncthreads();
+  cluster_arrive_release();
+  cluster_wait();  // phase 2: every store into this CTA has landed
   if (tid < rep) {
     float M = -INFINITY;
     for (int s2 = 0; s2 < S; ++s2)
@@ -337,16 +355,15 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
     for (int s2 = 0; s2 < S; ++s2) s_w[tid][s2] = s_cl[tid][s2] > 0.f ? exp2f(s_cm[tid][s2] - M) * inv : 0.f;
   }
   __syncthreads();
-  const int E = rep * D, e0 = split * E / S, e1 = (split + 1) * E / S;
+  const int e0 = split * E / S, e1 = (split + 1) * E / S;
   for (int e = e0 + tid; e < e1; e += kAW * 32) {
     const int hi = e / D, d = e % D;
     float num = 0.f;
     for (int s2 = 0; s2 < S; ++s2)
-      if (s_w[hi][s2] != 0.f) num = fmaf(ld_dsmem(c_num + hi * D + d, unsigned(s2)), s_w[hi][s2], num);
+      if (s_w[hi][s2] != 0.f) num = fmaf(s_rnum[s2 * slot_len + e - e0], s_w[hi][s2], num);
     Out[(h * rep + hi) * D + d] = __float2half_rn(num);
   }
-  // no CTA leaves while another may still read its shared memory
-  cluster_sync();
+  // no remote access follows phase 2: a CTA may leave
 }
 
 template <int D, bool FUSED>

@@ -143,17 +143,64 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_dl8_kernel(GemvDLArgs a, Sm
   if (!a.weights_static) grid_wait();
 #pragma unroll
   for (int s = 0; s < STAGES; ++s) issue(s);
+  // the RMSNorm weights of this thread's first activation item, likewise
+  const half* Gm = reinterpret_cast<const half*>(a.gamma);
+  const bool g16 = Gm && (reinterpret_cast<uintptr_t>(Gm) & 15) == 0;
+  uint4 gpre0 = make_uint4(0, 0, 0, 0), gpre1 = gpre0;
+  if (g16 && a.weights_static && tid < M * ng * 4) {
+    const uint4* gp = reinterpret_cast<const uint4*>(Gm + ((tid % (ng * 4)) >> 2) * 64 + (tid & 3) * 16);
+    gpre0 = __ldg(gp);
+    gpre1 = __ldg(gp + 1);
+  }
   grid_wait();
 
   // ------------------------------------------------ activation prologue
   {
+    // The activation rows are first copied into the xB area (row c at
+    // c * colstride words, element k at byte 2k) with all of this thread's
+    // loads in flight at once: one round trip to L2 instead of one per loop
+    // pass. Item (G, tt) below then reads its 32 bytes there and rewrites
+    // them in place as its MMA operand pairs (the same bytes, since both
+    // layouts put item (G, tt) at byte 128 G + 32 tt of the row). The
+    // arithmetic and its order are those of a direct read from global memory.
     const half* X = reinterpret_cast<const half*>(a.x);
-    const half* Gm = reinterpret_cast<const half*>(a.gamma);
+    unsigned char* xs = smem + L.xb_off;
+    const long rowb = long(L.colstride) * 4;
+    const int cpr = K / 8;  // 16-byte chunks per row
+    const int chunks = M * cpr;
+    if (((reinterpret_cast<uintptr_t>(X) | (uintptr_t(a.ldx) * 2)) & 15) == 0) {
+      for (int q0 = 0; q0 < chunks; q0 += 8 * kThreads) {
+        uint4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int q = q0 + j * kThreads + tid;
+          if (q < chunks) {
+            const int c = q / cpr, r = q - c * cpr;
+            v[j] = __ldcg(reinterpret_cast<const uint4*>(X + long(c) * a.ldx) + r);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int q = q0 + j * kThreads + tid;
+          if (q < chunks) {
+            const int c = q / cpr, r = q - c * cpr;
+            *reinterpret_cast<uint4*>(xs + c * rowb + r * 16) = v[j];
+          }
+        }
+      }
+    } else {
+      for (int q = tid; q < M * K; q += kThreads) {
+        const int c = q / K, k = q - c * K;
+        reinterpret_cast<half*>(xs + c * rowb)[k] = X[long(c) * a.ldx + k];
+      }
+    }
+    __syncthreads();
     if (Gm) {
       for (int c = 0; c < M; ++c) {
+        const half* xr_s = reinterpret_cast<const half*>(xs + c * rowb);
         float ss = 0.f;
         for (int k = tid; k < K; k += kThreads) {
-          const float v = __half2float(X[long(c) * a.ldx + k]);
+          const float v = __half2float(xr_s[k]);
           ss = fmaf(v, v, ss);
         }
 #pragma unroll
@@ -173,28 +220,51 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_dl8_kernel(GemvDLArgs a, Sm
       const int c = it / (ng * 4);
       const int rem = it - c * (ng * 4);
       const int G = rem >> 2, tt = rem & 3;
-      const half* xr = X + long(c) * a.ldx + G * 64;
-      const half* gr = Gm ? Gm + G * 64 : nullptr;
+      unsigned char* cell = xs + c * rowb + G * 128 + tt * 32;
+      uint4 raw[2];
+      raw[0] = *reinterpret_cast<const uint4*>(cell);
+      raw[1] = *reinterpret_cast<const uint4*>(cell + 16);
+      const half* xv = reinterpret_cast<const half*>(raw);
+      uint4 graw[2];
+      if (Gm) {
+        if (it == tid && g16 && a.weights_static) {
+          graw[0] = gpre0;
+          graw[1] = gpre1;
+        } else if (g16) {
+          const uint4* gp = reinterpret_cast<const uint4*>(Gm + G * 64 + tt * 16);
+          graw[0] = __ldg(gp);
+          graw[1] = __ldg(gp + 1);
+        } else {
+          half* gh = reinterpret_cast<half*>(graw);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) gh[i] = Gm[G * 64 + tt * 16 + i];
+        }
+      }
+      const half* gv = reinterpret_cast<const half*>(graw);
       const float inv = Gm ? s_inv[c] : 1.f;
       float bsum = 0.f, xsum = 0.f;
-      uint32_t* dst = xB + size_t(c) * L.colstride + (G * 4 + tt) * C::MP;
+      uint32_t outw[C::MP];
 #pragma unroll
       for (int p = 0; p < C::MP; ++p) {
         int k0, k1;
         bool hi;
         pair_k<4, 64>(tt, p, k0, k1, hi);
-        float x0 = __half2float(xr[k0]), x1 = __half2float(xr[k1]);
-        if (gr) {
-          x0 = rnd<half>(x0 * inv * __half2float(gr[k0]));
-          x1 = rnd<half>(x1 * inv * __half2float(gr[k1]));
+        k0 -= tt * 16;  // offsets within this item's 16 elements
+        k1 -= tt * 16;
+        float x0 = __half2float(xv[k0]), x1 = __half2float(xv[k1]);
+        if (Gm) {
+          x0 = rnd<half>(x0 * inv * __half2float(gv[k0]));
+          x1 = rnd<half>(x1 * inv * __half2float(gv[k1]));
         }
         xsum += x0 + x1;
         const float f = hi ? 0.0625f : 1.0f;
         const __half h0 = __float2half_rn(x0 * f), h1 = __float2half_rn(x1 * f);
         bsum += __half2float(h0) + __half2float(h1);
         __half2 hh = __halves2half2(h0, h1);
-        dst[p] = *reinterpret_cast<uint32_t*>(&hh);
+        outw[p] = *reinterpret_cast<uint32_t*>(&hh);
       }
+      *reinterpret_cast<uint4*>(cell) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
+      *reinterpret_cast<uint4*>(cell + 16) = make_uint4(outw[4], outw[5], outw[6], outw[7]);
       const unsigned mask = __activemask();
       bsum += __shfl_xor_sync(mask, bsum, 1);
       bsum += __shfl_xor_sync(mask, bsum, 2);
