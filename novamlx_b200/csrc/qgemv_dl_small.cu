@@ -13,11 +13,11 @@
 // each contributor writes its partial sums to its slot and the last to
 // arrive (shared-memory ticket) sums the slots in warp order. The grid is
 // chosen so that a tile group meets at most two CTAs (exactly one when there
-// are at most two tile groups per SM). A shared tile group is the start of
-// the later CTA's range, which finishes its part early and hands the sum
-// over (global scratch + release flag); the earlier CTA meets the tile group
-// at the end of its range, adds the handed-over sum (acquire, bounded wait)
-// and runs the epilogue. All sums have a fixed order, so results are
+// are at most two tile groups per SM). For a tile group two CTAs share, each
+// writes its part to its own global slot and takes a ticket; the second to
+// arrive adds the two parts and runs the epilogue, so no CTA waits for a
+// neighbour that started late. All sums have a fixed order (a sum of two
+// terms does not depend on which CTA adds them), so results are
 // deterministic.
 //
 // One activation row (ONE): the eight MMA columns are split between the two
@@ -76,20 +76,6 @@ __device__ __forceinline__ unsigned ordered_bits_s(float v) {
 // floor(k n / p)
 __host__ __device__ __forceinline__ int owner_of(long long i, long long n, long long p) {
   return int(((i + 1) * p - 1) / n);
-}
-
-__device__ __forceinline__ void flag_release(unsigned* f, unsigned v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
-}
-// waits (bounded) until *f is non-zero; false if it gave up
-__device__ __forceinline__ bool flag_acquire_wait(unsigned* f) {
-  for (unsigned it = 0; it < (1u << 24); ++it) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-    if (v) return true;
-    if (it > 64) __nanosleep(64);
-  }
-  return false;
 }
 
 template <int EPI, int TPT, int STAGES, bool ONE>
@@ -393,25 +379,29 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_dl8_kernel(GemvDLArgs a, Sm
     __syncwarp();
     if (fu == t0 && lu == t1 - 1) {
       finalize(T, mine);
-    } else if (fu > t0) {
-      // the CTA's first tile group, whose earlier part is the end of the
-      // previous CTA's range: hand this CTA's sum over (it is ready early)
-      float* part = a.partials + size_t(T) * (ROWS * NC);
-      for (int i = lane; i < ROWS * NC; i += 32) __stcg(part + i, mine[i]);
-      __syncwarp();
-      if (lane == 0) flag_release(a.counters + T, 1u);
     } else {
-      // the CTA's last tile group: the next CTA handed its part over at its
-      // start; add it (in that fixed order) and finish the tile group
-      unsigned ok = 1;
+      // a tile group shared with the neighbouring CTA (this CTA holds its
+      // start: side 1, or its end: side 0). Both publish their part; the
+      // second to arrive adds the two and finishes the tile group, so
+      // neither waits for the other. Two-term sums are order-free, so the
+      // result is the same whichever CTA finishes it.
+      const int side = fu > t0 ? 1 : 0;
+      float* slot = a.partials + (size_t(T) * 2 + side) * (ROWS * NC);
+      for (int i = lane; i < ROWS * NC; i += 32) __stcg(slot + i, mine[i]);
+      __threadfence();
+      __syncwarp();
+      unsigned last = 0;
       if (lane == 0) {
-        ok = flag_acquire_wait(a.counters + T);
-        if (!ok) atomicOr(a.err, 1u);
-        a.counters[T] = 0u;
+        last = atomicAdd(a.counters + T, 1u) == 1u ? 1u : 0u;
+        if (last) {
+          __threadfence();
+          a.counters[T] = 0u;  // zero again for the next launch
+        }
       }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      const float* part = a.partials + size_t(T) * (ROWS * NC);
-      for (int i = lane; i < ROWS * NC; i += 32) mine[i] += ok ? __ldcg(part + i) : 0.f;
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (!last) return;
+      const float* other = a.partials + (size_t(T) * 2 + (1 - side)) * (ROWS * NC);
+      for (int i = lane; i < ROWS * NC; i += 32) mine[i] += __ldcg(other + i);
       __syncwarp();
       finalize(T, mine);
     }
@@ -658,7 +648,7 @@ size_t qgemv_small_partials_floats(int N_out, int K, int epi, int num_sms) {
   (void)K;
   (void)num_sms;
   const int rows = epi == EPI_SILU ? 32 : 16;
-  return size_t(N_out / 16) * rows * 8;  // one hand-over slot per tile group
+  return size_t(N_out / 16) * rows * 8 * 2;  // two part slots per tile group
 }
 
 nmx_status_t qgemv_small(Ctx* c, const GemvDLArgs& a0, int epi) {
@@ -669,7 +659,7 @@ nmx_status_t qgemv_small(Ctx* c, const GemvDLArgs& a0, int epi) {
   const int stages = small_stages(a.M, a.K, tpt, grid, a.n_tg);
   const SmallLayout L = small_layout(a.M, a.K, tpt, stages, grid, a.n_tg);
   const int nc = a.M == 1 ? 1 : 8;
-  NMX_CHECK(size_t(a.n_tg) * 16 * tpt * nc <= a.partials_cap, NMX_ERR_UNSUPPORTED,
+  NMX_CHECK(size_t(a.n_tg) * 16 * tpt * nc * 2 <= a.partials_cap, NMX_ERR_UNSUPPORTED,
             "qgemv_small: partial-sum scratch too small");
   NMX_CHECK(a.err != nullptr, NMX_ERR_INVALID, "qgemv_small: no error word");
   return a.M == 1 ? by_epi<true>(c, a, epi, grid, stages, L) : by_epi<false>(c, a, epi, grid, stages, L);
