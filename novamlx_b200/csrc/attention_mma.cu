@@ -81,6 +81,8 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
   // numerators of this CTA's output slice, one row of slot_len per split
   __shared__ float s_rnum[kMaxRepA * D + kMaxClusterA];
   __shared__ float s_w[kMaxRepA][kMaxClusterA];
+  __shared__ float s_f[kAW + 1][kMaxRepA];  // per state and q head: exp2(m - M)
+  __shared__ float s_den[kMaxRepA];
   __shared__ __align__(16) half s_knew[D];
   __shared__ __align__(16) half s_vnew[D];
 
@@ -274,9 +276,10 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
       *reinterpret_cast<float2*>(s_o + (warp * kMaxRepA + g) * D + nt * 8 + 2 * t) = make_float2(o[nt][0], o[nt][1]);
     }
   }
-  if (warp == 0) {
-    // new token score per q head: f16 q · f16 k summed in f32, log2 units
-    for (int hi = 0; hi < rep; ++hi) {
+  {
+    // new token score per q head (warp w takes heads w, w + kAW): f16 q ·
+    // f16 k summed in f32, log2 units
+    for (int hi = warp; hi < rep; hi += kAW) {
       float sc = 0.f;
       if (owner) {
         for (int d = lane; d < D; d += 32) {
@@ -295,35 +298,41 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
   __syncthreads();
   grid_launch_dependents();
 
-  half* Out = reinterpret_cast<half*>(a.out) + long(row) * Hq * D;
-  for (int e = tid; e < rep * D; e += kAW * 32) {
-    const int hi = e / D, d = e % D;
+  // per q head (thread hi): the maximum over the warps' states and the new
+  // token, each state's factor exp2(m - M) and the denominator
+  if (tid < rep) {
+    const int hi = tid;
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w <= kAW; ++w)
       if (s_l[w][hi] > 0.f) M = fmaxf(M, s_m[w][hi]);
-    float num = 0.f, den = 0.f;
+    float den = 0.f;
 #pragma unroll
     for (int w = 0; w < kAW; ++w) {
-      if (s_l[w][hi] > 0.f) {
-        const float f = exp2f(s_m[w][hi] - M);
-        num = fmaf(s_o[(w * kMaxRepA + hi) * D + d], f, num);
-        den = fmaf(s_l[w][hi], f, den);
-      }
+      const float f = s_l[w][hi] > 0.f ? exp2f(s_m[w][hi] - M) : 0.f;
+      s_f[w][hi] = f;
+      if (s_l[w][hi] > 0.f) den = fmaf(s_l[w][hi], f, den);
     }
-    if (s_l[kAW][hi] > 0.f) {
-      const float f = exp2f(s_m[kAW][hi] - M);
-      num = fmaf(__half2float(s_vnew[d]), f, num);
-      den += f;
-    }
+    const float fn = s_l[kAW][hi] > 0.f ? exp2f(s_m[kAW][hi] - M) : 0.f;
+    s_f[kAW][hi] = fn;
+    if (s_l[kAW][hi] > 0.f) den += fn;
+    c_ml[hi][0] = M;
+    c_ml[hi][1] = den;
+  }
+  __syncthreads();
+  half* Out = reinterpret_cast<half*>(a.out) + long(row) * Hq * D;
+  for (int e = tid; e < rep * D; e += kAW * 32) {
+    const int hi = e / D, d = e % D;
+    float num = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAW; ++w)
+      if (s_l[w][hi] > 0.f) num = fmaf(s_o[(w * kMaxRepA + hi) * D + d], s_f[w][hi], num);
+    if (s_l[kAW][hi] > 0.f) num = fmaf(__half2float(s_vnew[d]), s_f[kAW][hi], num);
     if (S == 1) {
+      const float den = c_ml[hi][1];
       Out[(h * rep + hi) * D + d] = __float2half_rn(den > 0.f ? num / den : 0.f);
     } else {
       c_num[hi * D + d] = num;
-      if (d == 0) {
-        c_ml[hi][0] = M;
-        c_ml[hi][1] = den;
-      }
     }
   }
   if (S == 1) return;
@@ -344,21 +353,34 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
   }
   cluster_arrive_release();
   cluster_wait();  // phase 2: every store into this CTA has landed
-  if (tid < rep) {
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < S; ++s2)
-      if (s_cl[tid][s2] > 0.f) M = fmaxf(M, s_cm[tid][s2]);
-    float den = 0.f;
-    for (int s2 = 0; s2 < S; ++s2)
-      if (s_cl[tid][s2] > 0.f) den = fmaf(s_cl[tid][s2], exp2f(s_cm[tid][s2] - M), den);
-    const float inv = den > 0.f ? 1.f / den : 0.f;
-    for (int s2 = 0; s2 < S; ++s2) s_w[tid][s2] = s_cl[tid][s2] > 0.f ? exp2f(s_cm[tid][s2] - M) * inv : 0.f;
+  {
+    // the splits' weights, thread (hi, s2) = (tid / 16, tid % 16): the
+    // maximum over the head's live splits (a max of the half-warp), the
+    // factor exp2(m - M), then the denominator in split order (thread hi)
+    static_assert(kAW * 32 == kMaxRepA * kMaxClusterA, "one thread per (head, split)");
+    const int hi = tid >> 4, s2 = tid & 15;
+    const bool live = hi < rep && s2 < S && s_cl[hi][s2] > 0.f;
+    float M = live ? s_cm[hi][s2] : -INFINITY;
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    s_w[hi][s2] = live ? exp2f(s_cm[hi][s2] - M) : 0.f;
+    __syncthreads();
+    if (tid < rep) {
+      float den = 0.f;
+#pragma unroll 4
+      for (int k = 0; k < S; ++k)
+        if (s_cl[tid][k] > 0.f) den = fmaf(s_cl[tid][k], s_w[tid][k], den);
+      s_den[tid] = den > 0.f ? 1.f / den : 0.f;
+    }
+    __syncthreads();
+    if (live) s_w[hi][s2] *= s_den[hi];
+    __syncthreads();
   }
-  __syncthreads();
   const int e0 = split * E / S, e1 = (split + 1) * E / S;
   for (int e = e0 + tid; e < e1; e += kAW * 32) {
     const int hi = e / D, d = e % D;
     float num = 0.f;
+#pragma unroll 4
     for (int s2 = 0; s2 < S; ++s2)
       if (s_w[hi][s2] != 0.f) num = fmaf(s_rnum[s2 * slot_len + e - e0], s_w[hi][s2], num);
     Out[(h * rep + hi) * D + d] = __float2half_rn(num);

@@ -185,7 +185,15 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_dl8_kernel(GemvDLArgs a, Sm
       for (int c = 0; c < M; ++c) {
         const half* xr_s = reinterpret_cast<const half*>(xs + c * rowb);
         float ss = 0.f;
-        for (int k = tid; k < K; k += kThreads) {
+        int k = tid;
+        for (; k + 7 * kThreads < K; k += 8 * kThreads) {  // eight loads, then their FMAs in order
+          float v[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] = __half2float(xr_s[k + j * kThreads]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
+        }
+        for (; k < K; k += kThreads) {
           const float v = __half2float(xr_s[k]);
           ss = fmaf(v, v, ss);
         }
