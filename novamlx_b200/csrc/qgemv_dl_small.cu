@@ -57,8 +57,8 @@ struct SmallLayout {
   int c_max = 0;      // warps of one CTA a tile group can meet
 };
 
-__device__ __forceinline__ void cp16(void* smem_dst, const void* gsrc) {
-  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+// 16-byte copy to a shared-space address
+__device__ __forceinline__ void cp16(unsigned s, const void* gsrc) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gsrc) : "memory");
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
@@ -109,9 +109,11 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_dl8_kernel(GemvDLArgs a, Sm
   const unsigned char* src_cur = reinterpret_cast<const unsigned char*>(a.w) + size_t(u0) * kRecS + 16 * lane;
   const size_t pair_off = size_t(a.pair_tiles) * nb * kRecS;
   int is_u = u0;
-  auto issue = [&](int slot) {
+  // this lane's 16-byte slice of ring stage 0 (shared-space address)
+  const unsigned ring_s = static_cast<unsigned>(__cvta_generic_to_shared(ring)) + 16 * lane;
+  auto issue = [&](int slot_off) {  // slot_off: byte offset of the stage in the ring
     if (is_u < u1) {
-      unsigned char* dst = ring + size_t(slot) * TPT * kRecS + 16 * lane;
+      const unsigned dst = ring_s + unsigned(slot_off);
 #pragma unroll
       for (int tp = 0; tp < TPT; ++tp) {
         const unsigned char* src = src_cur + tp * pair_off;
@@ -128,7 +130,7 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_dl8_kernel(GemvDLArgs a, Sm
   // the wait (records an op-level caller may just have written are not)
   if (!a.weights_static) grid_wait();
 #pragma unroll
-  for (int s = 0; s < STAGES; ++s) issue(s);
+  for (int s = 0; s < STAGES; ++s) issue(s * TPT * kRecS);
   // the RMSNorm weights of this thread's first activation item, likewise
   const half* Gm = reinterpret_cast<const half*>(a.gamma);
   const bool g16 = Gm && (reinterpret_cast<uintptr_t>(Gm) & 15) == 0;
@@ -431,15 +433,22 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_dl8_kernel(GemvDLArgs a, Sm
   const int colsel = ONE ? 0 : (g < M ? g : M - 1);
   const unsigned char* xcol_b = xb_b + size_t(colsel) * L.colstride * 4 + t * 32;
 
-  int tg = u0 / nb, blk = u0 - (u0 / nb) * nb, slot = 0;
-  for (int u = u0; u < u1; ++u) {
+  // running state: tile group tg, the operand pointers of the current block
+  // (blk at the start), the ring stage's byte offset, and the unit that ends
+  // the current tile group's part of this warp's range
+  int tg = u0 / nb, slot_off = 0;
+  const int blk = u0 - tg * nb;
+  int seg_end = min(u1, (tg + 1) * nb);
+  const unsigned char* pa = xA_base + blk * xA_step;
+  const unsigned char* pb = xB_base + blk * xB_step;
+  const unsigned char* px = xcol_b + blk * 256;
+  int cxi = ONE ? 2 * blk + gi_t : blk * 16 + 2 * t;
+  for (int u = u0; u < u1;) {
     cp_wait<STAGES - 1>();
     __syncwarp();
-    const unsigned char* rec0 = ring + size_t(slot) * TPT * kRecS;
+    const unsigned char* rec0 = ring + slot_off;
     if constexpr (ONE) {
-      const float2 cx = CX[2 * blk + gi_t];
-      const unsigned char* pa = xA_base + blk * xA_step;
-      const unsigned char* pb = xB_base + blk * xB_step;
+      const float2 cx = CX[cxi];
       const uint4 xa0 = *reinterpret_cast<const uint4*>(pa);
       const uint4 xa1 = *reinterpret_cast<const uint4*>(pa + 16);
       const uint4 xb0 = *reinterpret_cast<const uint4*>(pb);
@@ -476,11 +485,9 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_dl8_kernel(GemvDLArgs a, Sm
     } else {
 #pragma unroll
       for (int gi = 0; gi < 2; ++gi) {
-        const int G = 2 * blk + gi;
-        const unsigned char* px = xcol_b + G * 128;
-        const uint4 xa = *reinterpret_cast<const uint4*>(px);
-        const uint4 xc = *reinterpret_cast<const uint4*>(px + 16);
-        const float4 cx = *reinterpret_cast<const float4*>(CX + G * 8 + 2 * t);
+        const uint4 xa = *reinterpret_cast<const uint4*>(px + gi * 128);
+        const uint4 xc = *reinterpret_cast<const uint4*>(px + gi * 128 + 16);
+        const float4 cx = *reinterpret_cast<const float4*>(CX + cxi + gi * 8);
 #pragma unroll
         for (int tp = 0; tp < TPT; ++tp) {
           const unsigned char* r = rec0 + tp * kRecS;
@@ -507,15 +514,22 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_dl8_kernel(GemvDLArgs a, Sm
       }
     }
     __syncwarp();
-    issue(slot);
-    if (blk == nb - 1 || u == u1 - 1) {
+    issue(slot_off);
+    slot_off = slot_off == (STAGES - 1) * TPT * kRecS ? 0 : slot_off + TPT * kRecS;
+    if (++u == seg_end) {
       flush(tg);
       zero_acc();
-    }
-    if (++slot == STAGES) slot = 0;
-    if (++blk == nb) {
-      blk = 0;
       ++tg;
+      seg_end = min(u1, seg_end + nb);
+      pa = xA_base;
+      pb = xB_base;
+      px = xcol_b;
+      cxi = ONE ? gi_t : 2 * t;
+    } else {
+      pa += xA_step;
+      pb += xB_step;
+      px += 256;
+      cxi += ONE ? 2 : 16;
     }
   }
   cp_wait<0>();
