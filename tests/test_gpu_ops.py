@@ -185,6 +185,25 @@ def test_qmatmul_records_deterministic(env, M, N, K):
         assert np.array_equal(y, ys[0])
 
 
+@pytest.mark.parametrize("M,N,K", [(1, 6144, 4096), (3, 4096, 14336), (8, 512, 1024)])
+def test_qmatmul_records_unaligned_activations(env, M, N, K):
+    """Activations at an address that is not 16-byte aligned are staged
+    element by element: the same bits as the aligned call."""
+    torch, nmx, ctx = env
+    rng = np.random.default_rng(N + 3 * K + M)
+    w = rng.standard_normal((N, K), dtype=np.float32) * 0.02
+    wq, s, b = O.quantize(w, 4, 64)
+    xd = u16(torch, O.f32_to_f16bits(rng.standard_normal((M, K), dtype=np.float32)))
+    buf = torch.zeros(M * K + 8, dtype=xd.dtype, device=xd.device)
+    xm = buf[1:1 + M * K].view(M, K)
+    xm.copy_(xd)
+    assert xm.data_ptr() % 16 != 0
+    rec = ctx.pack_records(dev(torch, wq.view(np.int32)), u16(torch, s), u16(torch, b))
+    y0 = host16(ctx.quantized_matmul_records(xd, rec, N))
+    y1 = host16(ctx.quantized_matmul_records(xm, rec, N))
+    assert np.array_equal(y0, y1)
+
+
 def test_qmatmul_records_rejects_tiny(env):
     """Fewer than eight (tile group, block) units: not served by the records kernel."""
     torch, nmx, ctx = env
