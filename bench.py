@@ -138,11 +138,21 @@ def host_model_8b(seed: int = 0):
     return O.OracleModel(cfg, t)
 
 
+def host_threads() -> int:
+    """Every host core this process may run on, whatever OMP_NUM_THREADS the
+    launcher set (torch.distributed.run sets 1)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_decode_sample(max_seconds: float, min_tokens: int, max_tokens: int, seed: int = 0):
     """Times the CPU restatement's decode step at context 2048 (random KV of
     the right size; a CPU prefill of 2048 tokens would take tens of minutes).
     Returns (tok/s, tokens, seconds, threads)."""
     from oracle import oracle as O
+    O.set_threads(host_threads())
     om = host_model_8b(seed)
     kc, vc, cap = om.new_cache(PROMPT + max_tokens + 8)
     rng = np.random.default_rng(seed + 1)
@@ -164,6 +174,7 @@ def run_reference(args, rank: int, world: int) -> None:
     if rank != 0:
         return
     from oracle import oracle as O
+    O.set_threads(host_threads())
     om = host_model_8b(0)
     kc, vc, cap = om.new_cache(PROMPT + args.warmup + args.steps + 8)
     rng = np.random.default_rng(1)

@@ -72,7 +72,18 @@ NMX_API nmx_status_t nmx_ctx_destroy(nmx_ctx_t ctx);
 /* Use an external cudaStream_t (passed as void*) instead of the owned one. */
 NMX_API nmx_status_t nmx_ctx_set_stream(nmx_ctx_t ctx, void* cuda_stream);
 NMX_API void* nmx_ctx_stream(nmx_ctx_t ctx);
+/* Waits for the context's stream; NMX_ERR_TIMEOUT if a kernel gave up a
+ * bounded device-side wait since the last check (the error is then cleared
+ * and the results of that work are not valid). */
 NMX_API nmx_status_t nmx_ctx_synchronize(nmx_ctx_t ctx);
+/* Polls a device-side wait makes before it gives up and reports
+ * NMX_ERR_TIMEOUT (peer-rank exchange flags, the pipeline barriers of the
+ * tensor-core GEMMs, the K shares of a split GEMM); 0 restores the default
+ * (2^24 polls, seconds). Every wait is bounded, so a rank that never
+ * publishes, or a fault elsewhere, ends the kernel instead of holding the
+ * GPU. Takes effect for kernels launched after the call (stream order). No
+ * counterpart in the reference, whose MLX calls have no device waits. */
+NMX_API nmx_status_t nmx_ctx_set_wait_limit(nmx_ctx_t ctx, uint32_t polls);
 /* Number of kernels this library launched on the context so far (graph
  * replays count every node). Used by benchmarks to report launches. */
 NMX_API uint64_t nmx_ctx_kernel_launches(nmx_ctx_t ctx);
@@ -179,6 +190,7 @@ NMX_API nmx_status_t nmx_op_attn_quantized_decode(
  * sequence, GQA). q [B, Hq, D] f16; k_cache/v_cache are the pool's layer
  * views returned by nmx_kv_pool_layer_ptrs; block_tables int32[B, max_blocks];
  * seq_lens int32[B] (keys 0..seq_lens-1 are attended). out [B, Hq, D] f16.
+ * At most 65535 rows per call (NMX_ERR_UNSUPPORTED beyond).
  * Replaces MLXFast.scaledDotProductAttention over KVCacheSimple for L == 1
  * (call sites Sources/NovaMLXEngine/FusedBatchScheduler.swift:1215 via
  * mlx-swift-lm AttentionUtils). */
@@ -191,15 +203,15 @@ NMX_API nmx_status_t nmx_op_attn_paged_decode(nmx_ctx_t ctx, const void* q, cons
 /* The same decode attention as nmx_op_attn_paged_decode, for callers that
  * cannot allocate device memory (a host that reserves its whole device
  * budget up front and admits work against it, or one that cannot afford the
- * device synchronisation cudaMalloc/cudaFree may cause). Its scratch (split
- * partial sums, tickets, row descriptors) lives in a fixed 8 MiB array inside
- * the library, held on every GPU that loads it until exit; it never
- * allocates. The first call on a device looks up that array's address with
- * the device current; make it before any stream capture. Calls share the
- * array: calls that overlap on the GPU race. It uses fewer key splits than
- * nmx_op_attn_paged_decode when they would not fit (results can then differ
- * in the last bits) and returns NMX_ERR_UNSUPPORTED when even one split does
- * not fit. No counterpart in the reference. */
+ * device synchronisation cudaMalloc/cudaFree may cause). Its only scratch,
+ * the per-row descriptors (8 bytes per row), lives in a fixed 256 KiB array
+ * inside the library, held on every GPU that loads it until exit; it never
+ * allocates. At most 32768 rows per call: larger batches return
+ * NMX_ERR_UNSUPPORTED before anything is launched. Same key splits and the
+ * same bits as nmx_op_attn_paged_decode. The first call on a device looks up
+ * that array's address with the device current; make it before any stream
+ * capture. Calls share the array: calls that overlap on the GPU race. No
+ * counterpart in the reference. */
 NMX_API nmx_status_t nmx_op_attn_paged_decode_noalloc(nmx_ctx_t ctx, const void* q,
                                                       const void* k_cache, const void* v_cache,
                                                       const int32_t* block_tables,
@@ -272,13 +284,6 @@ NMX_API uint64_t nmx_model_weight_bytes(nmx_model_t model);
 /* Bytes the weights of one decode step read (every linear once, one
  * embedding row, norms). */
 NMX_API uint64_t nmx_model_step_weight_bytes(nmx_model_t model);
-/* Batch-1 decode schedule (no counterpart in the reference, which has no
- * kernel schedule to choose): enable != 0 runs batch-1 nmx_decode_greedy,
- * and batch-1 nmx_forward decode steps that return ids, as one persistent
- * cooperative launch; 0 (the default) uses one CUDA graph of per-layer
- * kernels per step. Both give the same ids up to floating-point summation
- * order. */
-NMX_API nmx_status_t nmx_model_set_persistent_decode(nmx_model_t model, int enable);
 
 /* Paged KV pool: num_blocks blocks of block_tokens tokens, fp16 K and V for
  * every layer. Layout per layer: [num_blocks][Hkv][block_tokens][head_dim]

@@ -39,9 +39,13 @@ nmx_status_t ctx_check_device_error(Ctx* c) {
   NMX_CUDA_OK(cudaMemcpy(&v, c->dev_err, sizeof(v), cudaMemcpyDeviceToHost));
   if (v != 0) {
     NMX_CUDA_OK(cudaMemset(c->dev_err, 0, sizeof(v)));
-    set_error("a kernel gave up a bounded wait (device error word " + std::to_string(v) + "); results of the "
-              "work since the last check are not valid");
-    return NMX_ERR_CUDA;
+    std::string what;
+    if (v & kErrPeerWait) what += " a peer rank's exchange flag;";
+    if (v & kErrPipeWait) what += " a tensor-core GEMM pipeline barrier;";
+    if (v & kErrShareWait) what += " the K shares of a split GEMM;";
+    set_error("a bounded device wait ran out (device error word " + std::to_string(v) + ":" + what +
+              ") results of the work since the last check are not valid");
+    return NMX_ERR_TIMEOUT;
   }
   return NMX_OK;
 }
@@ -102,6 +106,7 @@ NMX_API nmx_status_t nmx_ctx_create(int device, nmx_ctx_t* out) {
   h->c.owns_stream = true;
   e = cudaMalloc(reinterpret_cast<void**>(&h->c.dev_err), 256);
   if (e == cudaSuccess) e = cudaMemset(h->c.dev_err, 0, 256);
+  if (e == cudaSuccess) e = cudaMemcpy(h->c.dev_err + 1, &kDefaultWaitPolls, 4, cudaMemcpyHostToDevice);
   if (e != cudaSuccess) {
     cudaGetLastError();
     if (h->c.dev_err) cudaFree(h->c.dev_err);
@@ -160,6 +165,17 @@ NMX_API nmx_status_t nmx_ctx_synchronize(nmx_ctx_t ctx) {
   REQUIRE(ctx, "context");
   NMX_CUDA_OK(cudaStreamSynchronize(ctx->c.stream));
   return ctx_check_device_error(&ctx->c);
+}
+
+NMX_API nmx_status_t nmx_ctx_set_wait_limit(nmx_ctx_t ctx, uint32_t polls) {
+  API_BEGIN;
+  REQUIRE(ctx, "context");
+  // the value travels with the stream, so kernels already queued keep theirs
+  static thread_local uint32_t v;
+  v = polls == 0 ? kDefaultWaitPolls : polls;
+  NMX_CUDA_OK(cudaMemcpyAsync(ctx->c.dev_err + 1, &v, 4, cudaMemcpyHostToDevice, ctx->c.stream));
+  NMX_CUDA_OK(cudaStreamSynchronize(ctx->c.stream));
+  return NMX_OK;
 }
 
 NMX_API uint64_t nmx_ctx_kernel_launches(nmx_ctx_t ctx) { return ctx ? ctx->c.launches : 0; }
@@ -339,23 +355,20 @@ NMX_API nmx_status_t nmx_op_attn_paged_decode(nmx_ctx_t ctx, const void* q, cons
   REQUIRE(seq_lens, "seq_lens");
   REQUIRE(out, "out");
   NMX_CHECK(Hkv > 0 && Hq % Hkv == 0, NMX_ERR_INVALID, "paged decode: Hq must be a multiple of Hkv");
+  NMX_CHECK(B > 0 && B <= kMaxDecodeRows, NMX_ERR_UNSUPPORTED,
+            "paged decode: at most " + std::to_string(kMaxDecodeRows) + " rows per call");
   Ctx* c = &ctx->c;
-  const int S = std::max(1, std::min(32, (2 * c->num_sms + B * Hkv - 1) / (B * Hkv)));
-  // workspace: tok_seq[B], tok_pos[B], partials
-  const size_t n_o = size_t(B) * Hq * S * D, n_ml = size_t(B) * Hq * S * 2;
+  const int S = decode_attn_splits(c->num_sms, B, Hkv);
+  // workspace: the row descriptors tok_seq[B], tok_pos[B]
   void* ws = nullptr;
-  NMX_TRY(ctx_workspace(c, (n_o + n_ml) * 4 + size_t(B) * 8 + 256, &ws));
-  unsigned* ctr = nullptr;
-  NMX_TRY(ctx_counters(c, size_t(B) * Hkv, &ctr));
-  float* part_o = static_cast<float*>(ws);
-  float* part_ml = part_o + n_o;
-  int* tok_seq = reinterpret_cast<int*>(part_ml + n_ml);
+  NMX_TRY(ctx_workspace(c, size_t(B) * 8, &ws));
+  int* tok_seq = static_cast<int*>(ws);
   int* tok_pos = tok_seq + B;
   NMX_TRY(seq_rows_from_lens(c, seq_lens, B, tok_seq, tok_pos));
   AttnArgs a;
   a.q = q; a.ldq = long(Hq) * D; a.k_cache = const_cast<void*>(k_cache); a.v_cache = const_cast<void*>(v_cache);
   a.block_tables = block_tables; a.max_blocks = max_blocks; a.tok_seq = tok_seq; a.tok_pos = tok_pos;
-  a.out = out; a.part_o = part_o; a.part_ml = part_ml; a.counters = ctr;
+  a.out = out;
   a.T = B; a.Hq = Hq; a.Hkv = Hkv; a.D = D; a.BT = block_tokens; a.splits = S; a.scale = scale;
   return paged_attention(c, a, false);
 }
@@ -408,13 +421,6 @@ NMX_API nmx_status_t nmx_model_get_tensor(nmx_model_t model, const char* name, v
 
 NMX_API uint64_t nmx_model_weight_bytes(nmx_model_t model) { return model ? model->m->wbytes : 0; }
 NMX_API uint64_t nmx_model_step_weight_bytes(nmx_model_t model) { return model ? model->m->step_bytes : 0; }
-
-NMX_API nmx_status_t nmx_model_set_persistent_decode(nmx_model_t model, int enable) {
-  API_BEGIN;
-  REQUIRE(model, "model");
-  model->m->persistent_enabled = enable != 0;
-  return NMX_OK;
-}
 
 NMX_API nmx_status_t nmx_kv_pool_create(nmx_model_t model, int block_tokens, int num_blocks, nmx_kv_pool_t* out) {
   API_BEGIN;

@@ -147,6 +147,8 @@ nmx_status_t paged_attention(Ctx* c, const AttnArgs& a, bool fused) {
   NMX_CHECK(a.Hkv > 0 && a.Hq % a.Hkv == 0 && a.Hq / a.Hkv <= kMaxRep, NMX_ERR_UNSUPPORTED,
             "paged attention: q heads per kv head must be <= 8");
   NMX_CHECK(a.splits >= 1, NMX_ERR_INVALID, "paged attention: splits >= 1");
+  NMX_CHECK(a.T >= 0 && a.T <= kMaxDecodeRows, NMX_ERR_UNSUPPORTED,
+            "paged attention: at most " + std::to_string(kMaxDecodeRows) + " query rows per call");
   if (a.T == 0) return NMX_OK;
   return paged_attention_mma(c, a, fused);
 }

@@ -36,7 +36,7 @@ namespace {
 constexpr int kAW = 4;        // warps per CTA
 constexpr int kAStages = 2;   // cp.async stages per warp
 constexpr int kMaxRepA = 8;   // q heads per kv head
-constexpr int kMaxClusterA = 16;  // key splits per (row, kv head): one cluster
+constexpr int kMaxClusterA = kMaxDecodeSplits;  // key splits per (row, kv head): one cluster
 
 __device__ __forceinline__ unsigned cluster_rank() {
   unsigned r;

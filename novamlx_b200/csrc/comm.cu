@@ -24,8 +24,9 @@
 // Two regions suffice: a rank writes R0 again only in the next layer, after
 // it passed the down_proj exchange, which every peer entered only after
 // finishing its reads of R0. Epochs only grow, so flags never need resetting.
-// A wait that runs out sets bit 0 of *err and skips the sum; the host reads it
-// with the step's results. Only plain loads and stores touch peer memory.
+// A wait that runs out (after the context's poll limit) sets kErrPeerWait in
+// *err and skips the sum; the host reads it with the step's results and
+// reports NMX_ERR_TIMEOUT. Only plain loads and stores touch peer memory.
 #include <cstring>
 #include <vector>
 
@@ -39,7 +40,6 @@ namespace nmx {
 namespace {
 
 constexpr int kARThreads = 256;
-constexpr unsigned kARSpin = 1u << 24;
 
 struct ARArgs {
   const half* part[kMaxRanks];      // the region on every rank (this rank's included)
@@ -76,12 +76,13 @@ __global__ void __launch_bounds__(kARThreads) allreduce_resid_kernel(ARArgs a) {
       for (int q = 0; q < a.world; ++q) st_release_sys(a.peer_flag[q], e);
     }
     int ok = 1;
+    const unsigned lim = wait_polls(a.err);
     for (int q = 0; q < a.world && ok; ++q) {
       unsigned it = 0;
       while ((int)(ld_acquire_sys(a.my_flags + q) - e) < 0) {
-        if (++it >= kARSpin) {
+        if (++it >= lim) {
           ok = 0;
-          atomicOr(a.err, 1u);
+          atomicOr(a.err, kErrPeerWait);
           break;
         }
       }

@@ -61,13 +61,25 @@ struct Ctx {
   size_t ws_bytes = 0;
   unsigned* counters = nullptr;  // zeroed, reset by kernels after use
   size_t n_counters = 0;
-  // device word that kernels set when a bounded wait runs out (bit 0);
-  // read and cleared by nmx_ctx_synchronize
+  // device words: [0] error bits that kernels set when a bounded wait runs
+  // out (read and cleared with each step's results and by
+  // nmx_ctx_synchronize); [1] the number of polls a wait makes before it
+  // gives up (nmx_ctx_set_wait_limit)
   unsigned* dev_err = nullptr;
 };
 
+// error bits of the device word: which kind of bounded wait ran out
+constexpr unsigned kErrPeerWait = 1u;   // a peer rank's exchange flag (tensor parallelism)
+constexpr unsigned kErrPipeWait = 2u;   // a pipeline barrier inside a tensor-core GEMM
+constexpr unsigned kErrShareWait = 4u;  // the K shares of a split GEMM tile group
+constexpr unsigned kDefaultWaitPolls = 1u << 24;
+// the poll limit the host set for this context (one load per kernel)
+__device__ __forceinline__ unsigned wait_polls(const unsigned* err) {
+  return reinterpret_cast<const volatile unsigned*>(err)[1];
+}
+
 nmx_status_t ctx_workspace(Ctx* c, size_t bytes, void** out);
-// after the stream has drained: NMX_ERR_CUDA if a kernel reported a wait
+// after the stream has drained: NMX_ERR_TIMEOUT if a kernel reported a wait
 // that ran out (the word is cleared)
 nmx_status_t ctx_check_device_error(Ctx* c);
 nmx_status_t ctx_counters(Ctx* c, size_t n, unsigned** out);

@@ -92,6 +92,7 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
   __shared__ int s_fail;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const unsigned lim = wait_polls(a.err);  // polls before a pipeline wait gives up
   const int m0 = blockIdx.x * kTM;
   const int nt = blockIdx.y;  // output tile
   const int KT = a.K / kTK, nb = a.K / 128;
@@ -126,8 +127,8 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
     if (lane == 0) {
       for (int b = 0; b < nb; ++b) {
         const int rs = b % kRS;
-        if (b >= kRS && !mbar_wait(&raw_empty[rs], ((b / kRS) - 1) & 1)) {
-          atomicOr(a.err, 1u);
+        if (b >= kRS && !mbar_wait(&raw_empty[rs], ((b / kRS) - 1) & 1, lim)) {
+          atomicOr(a.err, kErrPipeWait);
           s_fail = 1;
           break;
         }
@@ -149,8 +150,8 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
     if (lane == 0) {
       for (int kt = 0; kt < KT; ++kt) {
         const int s = kt % kTS;
-        if (kt >= kTS && !mbar_wait(&empty[s], ((kt / kTS) - 1) & 1)) {
-          atomicOr(a.err, 1u);
+        if (kt >= kTS && !mbar_wait(&empty[s], ((kt / kTS) - 1) & 1, lim)) {
+          atomicOr(a.err, kErrPipeWait);
           s_fail = 1;
           break;
         }
@@ -172,8 +173,8 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
       constexpr uint32_t kStageD = kStageBytes >> 4, kAD = kABytes >> 4;
       for (int kt = 0; kt < KT; ++kt) {
         const int s = kt % kTS;
-        if (!mbar_wait(&full[s], (kt / kTS) & 1)) {
-          atomicOr(a.err, 1u);
+        if (!mbar_wait(&full[s], (kt / kTS) & 1, lim)) {
+          atomicOr(a.err, kErrPipeWait);
           s_fail = 1;
           break;
         }
@@ -191,15 +192,15 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
     // ----------------------------------------- dequant warps: weight tile rows
     for (int kt = 0; kt < KT; ++kt) {
       const int s = kt % kTS;
-      if (kt >= kTS && !mbar_wait(&empty[s], ((kt / kTS) - 1) & 1)) {
-        atomicOr(a.err, 1u);
+      if (kt >= kTS && !mbar_wait(&empty[s], ((kt / kTS) - 1) & 1, lim)) {
+        atomicOr(a.err, kErrPipeWait);
         s_fail = 1;
         break;
       }
       unsigned char* B = smem + s * kStageBytes + kABytes;
       const int blk = kt >> 1, gi = kt & 1, rs = blk % kRS;
-      if (gi == 0 && !mbar_wait(&raw_full[rs], (blk / kRS) & 1)) {
-        atomicOr(a.err, 1u);
+      if (gi == 0 && !mbar_wait(&raw_full[rs], (blk / kRS) & 1, lim)) {
+        atomicOr(a.err, kErrPipeWait);
         s_fail = 1;
         break;
       }
@@ -234,8 +235,8 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
     }
 
     // ------------------------------------------------------------ epilogue
-    if (!s_fail && !mbar_wait(&acc_bar, 0)) {
-      atomicOr(a.err, 1u);
+    if (!s_fail && !mbar_wait(&acc_bar, 0, lim)) {
+      atomicOr(a.err, kErrPipeWait);
       s_fail = 1;
     }
     tc_fence_after();

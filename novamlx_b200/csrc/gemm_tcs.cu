@@ -68,7 +68,6 @@ using tc::kRecPad;                          // shared-memory stride of a record
 constexpr int kRawSlot = 8 * kRecPad;       // the 8 records of one tile and K block
 constexpr int kMaxTG = 16;                  // weight tiles per CTA
 constexpr int kMaxNT = 128;
-constexpr unsigned kShareSpin = 1u << 22;  // polls of the group counter before giving up
 constexpr size_t kSmemCap = 225 * 1024;  // dynamic shared memory the kernel may ask for (plus 1 KB static)
 
 struct TcsArgs {
@@ -129,7 +128,6 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-constexpr unsigned kXSpin = 1u << 24;
 
 // Fused exchange: this CTA's partial rows are in its region; publish slot
 // `slot` at epoch e to every rank and wait (bounded) until every rank has
@@ -140,12 +138,13 @@ __device__ __forceinline__ bool tp_exchange(const ExchangeArgs& x, int slot, uns
   if (threadIdx.x == 0) {
     for (int q = 0; q < x.world; ++q) st_release_sys(x.peer_tflags[q] + slot, e);
     int ok = 1;
+    const unsigned lim = wait_polls(err);
     for (int q = 0; q < x.world && ok; ++q) {
       unsigned it = 0;
       while ((int)(ld_acquire_sys(x.my_tflags + size_t(q) * kMaxTileFlags + slot) - e) < 0)
-        if (++it >= kXSpin) {
+        if (++it >= lim) {
           ok = 0;
-          atomicOr(err, 1u);
+          atomicOr(err, kErrPeerWait);
           break;
         }
     }
@@ -247,6 +246,7 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
   __shared__ int s_xok;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const unsigned lim = wait_polls(a.err);  // polls before a wait gives up
   const int grp = blockIdx.x, share = blockIdx.y;
   const int t0 = grp * a.tg;
   const int ntl = min(a.tg, a.n_atiles - t0);  // weight tiles of this CTA
@@ -293,8 +293,8 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
       // division per unit would cost more than the unit's issue work
       int rs = 0, rph = 0, b = b0, ti = 0;
       for (int i = 0; i < units; ++i) {
-        if (i >= a.rs && !mbar_wait(&raw_empty[rs], rph ^ 1)) {
-          atomicOr(a.err, 1u);
+        if (i >= a.rs && !mbar_wait(&raw_empty[rs], rph ^ 1, lim)) {
+          atomicOr(a.err, kErrPipeWait);
           s_fail = 1;
           break;
         }
@@ -316,8 +316,8 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
     if (lane == 0) {
       int xs = 0, xph = 0;
       for (int bi = 0; bi < nblk; ++bi) {
-        if (bi >= a.xs && !mbar_wait(&x_empty[xs], xph ^ 1)) {
-          atomicOr(a.err, 1u);
+        if (bi >= a.xs && !mbar_wait(&x_empty[xs], xph ^ 1, lim)) {
+          atomicOr(a.err, kErrPipeWait);
           s_fail = 1;
           break;
         }
@@ -347,10 +347,10 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
       int ti = 0, as = 0, aph = 0, xs = 0, xph = 0;
       uint32_t first = 0u;  // 0 until the first block is in the accumulators
       for (int i = 0; i < units; ++i) {
-        bool ok = !(ti == 0 && !mbar_wait(&x_full[xs], xph));
-        if (ok && !mbar_wait(&a_full[as], aph)) ok = false;
+        bool ok = !(ti == 0 && !mbar_wait(&x_full[xs], xph, lim));
+        if (ok && !mbar_wait(&a_full[as], aph, lim)) ok = false;
         if (!ok) {
-          atomicOr(a.err, 1u);
+          atomicOr(a.err, kErrPipeWait);
           s_fail = 1;
           break;
         }
@@ -393,13 +393,13 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
     const int as = dg;
     int rs = dg % a.rs, rph = (dg / a.rs) & 1;
     for (int i = dg; i < units; i += kDG) {
-      if (i >= kAST && !mbar_wait(&a_empty[as], ((i / kAST) - 1) & 1)) {
-        atomicOr(a.err, 1u);
+      if (i >= kAST && !mbar_wait(&a_empty[as], ((i / kAST) - 1) & 1, lim)) {
+        atomicOr(a.err, kErrPipeWait);
         s_fail = 1;
         break;
       }
-      if (!mbar_wait(&raw_full[rs], rph)) {
-        atomicOr(a.err, 1u);
+      if (!mbar_wait(&raw_full[rs], rph, lim)) {
+        atomicOr(a.err, kErrPipeWait);
         s_fail = 1;
         break;
       }
@@ -434,8 +434,8 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
     }
 
     // ------------------------------------------------------------ epilogue
-    if (!mbar_wait(&acc_bar, 0)) {
-      atomicOr(a.err, 1u);
+    if (!mbar_wait(&acc_bar, 0, lim)) {
+      atomicOr(a.err, kErrPipeWait);
       s_fail = 1;
     }
     tc::tc_fence_after();
@@ -503,13 +503,13 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
         unsigned* ctr = a.counters + grp;
         atomicAdd(ctr, 1u);
         unsigned v = 0;
-        for (unsigned it = 0; it < kShareSpin; ++it) {
+        for (unsigned it = 0; it < lim; ++it) {
           asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
           if (v >= unsigned(a.S)) break;
           __nanosleep(64);
         }
         s_last = v >= unsigned(a.S) ? 1u : 0u;
-        if (!s_last) atomicOr(a.err, 1u);
+        if (!s_last) atomicOr(a.err, kErrShareWait);
       }
       dq_bar();
       // this share's slice of the group's outputs, 4 rows per item, partials

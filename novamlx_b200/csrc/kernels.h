@@ -125,9 +125,6 @@ struct AttnArgs {
   const int* tok_pos = nullptr;  // [T] absolute position of each query row
   const float* inv_freq = nullptr;  // [D/2] (FUSED only)
   void* out = nullptr;         // [T, Hq*D]
-  float* part_o = nullptr;     // [T][Hq][S][D]
-  float* part_ml = nullptr;    // [T][Hq][S][2]
-  unsigned* counters = nullptr;  // [T][Hkv]
   int T = 0, Hq = 0, Hkv = 0, D = 0, BT = 16;
   int splits = 1;
   float scale = 1.0f;
@@ -135,63 +132,22 @@ struct AttnArgs {
   // (true in the decode step): the K/V stream may start before its wait
   bool kv_static = false;
 };
-// ------------------------------------------------ persistent batch-1 decode
-// (decode_persistent.cu): the phases of one decode step, run back to back by
-// one cooperative launch with a grid barrier after each phase.
-enum PhaseKind { PH_EMBED = 0, PH_GEMV = 1, PH_ATTN = 2, PH_COMBINE = 3, PH_ADVANCE = 4 };
-struct PPhase {
-  int kind = 0;
-  int epi = 0, tpt = 1;          // GEMV epilogue; records per unit (2: gate + up)
-  int n_tg = 0, K = 0, G = 0;    // GEMV tile groups, k, CTAs that take part
-  int lt_max = 0, c_max = 0;     // GEMV: tile groups per CTA range, warps per tile group (bounds)
-  int layer = 0;                 // ATTN: layer of the KV pool
-  long long pair_off = 0;        // GEMV SiLU: bytes from a gate record to its up record
-  const unsigned char* w = nullptr;  // GEMV decode records
-  const half* x = nullptr;       // GEMV input row
-  const half* gamma = nullptr;   // GEMV RMSNorm weight (null: none)
-  const half* bias = nullptr;    // GEMV output bias
-  half* y = nullptr;             // GEMV output row
-  const half* res = nullptr;     // GEMV residual (EPI_RESID)
-};
-struct PersistArgs {
-  const PPhase* ph = nullptr;
-  int n_ph = 0, steps = 0;
-  int* tok_ids = nullptr;        // [1] token of the step (advanced in place)
-  int* tok_pos = nullptr;        // [1] its position (advanced in place)
-  int* hist = nullptr;           // [hist_cap] ids of the steps
-  int hist_cap = 0;
-  int* step = nullptr;           // history cursor
-  int* out_id = nullptr;         // optional: id of the step
-  const int* table = nullptr;    // block table of the sequence
-  char* kv_base = nullptr;       // KV pool: layer l K at kv_base + l * stride, V half a stride on
-  size_t kv_layer_stride = 0;
-  int Hq = 0, Hkv = 0, D = 0, S = 0;  // heads, head_dim, key splits per kv head
-  float scale = 1.f;
-  const float* inv_freq = nullptr;
-  float eps = 1e-5f;
-  const half* embed = nullptr;
-  int H = 0;
-  half* h = nullptr;             // residual stream
-  const half* qkv = nullptr;
-  half* attn = nullptr;
-  float* part_o = nullptr;       // [Hkv * S][rep][D]
-  float* part_ml = nullptr;      // [Hkv * S][rep][2]
-  unsigned* flags = nullptr;     // [max n_tg] GEMV hand-over flags, zero between phases
-  float* hand = nullptr;         // [max n_tg][32] hand-over sums
-  unsigned long long* best = nullptr;  // [grid] argmax keys
-  unsigned* err = nullptr;
-  unsigned* bar = nullptr;       // [2] arrival count, generation
-  int off_xb = 0, off_cx = 0, off_wout = 0, off_red = 0, off_cnt = 0, off_zero = 0;
-};
-// red_slots: the largest lt_max * c_max of the phases
-size_t persist_smem_bytes(int K_max, int red_slots, int lt_max, int D);
-nmx_status_t persist_layout(int K_max, int red_slots, int lt_max, PersistArgs* A);
-int persist_warps();
-nmx_status_t persist_launch(Ctx* c, const PersistArgs& A, size_t smem);
 
 // fused = 1: apply RoPE to q and append the row's own k/v (one query row per
 // sequence, decode); fused = 0: q is already roped and K/V already appended.
+// The splits of one (row, kv head) are one thread-block cluster and combine
+// through distributed shared memory: no global scratch beyond the row
+// descriptors. At most kMaxDecodeRows rows (the grid's z extent).
+constexpr int kMaxDecodeSplits = 16;
+constexpr long kMaxDecodeRows = 65535;
 nmx_status_t paged_attention(Ctx* c, const AttnArgs& a, bool fused);
+// key splits per (row, kv head): enough CTAs for two per SM, at most one
+// cluster
+inline int decode_attn_splits(int num_sms, long rows, int Hkv) {
+  const long units = rows * long(Hkv > 0 ? Hkv : 1);
+  const long s = (2L * num_sms + units - 1) / units;
+  return int(s < 1 ? 1 : (s > kMaxDecodeSplits ? kMaxDecodeSplits : s));
+}
 // prefill chunks / mixed batches: query blocks of up to 16 rows of one
 // sequence (attention_prefill.cu). prefill_items cuts the batch's rows
 // (row_seq: sequence of each row, rows of a sequence consecutive) into

@@ -36,7 +36,6 @@ namespace {
 
 constexpr int kBT = 16;             // tokens per KV block
 constexpr int kBlockCap = 4096;     // block-table columns per sequence (65,536 tokens)
-constexpr int kMaxSplits = 16;      // split-KV CTAs per (sequence, kv head): one cluster
 constexpr int kHistCap = 1 << 16;   // decode-loop id history entries
 
 size_t dsize(nmx_dtype_t dt) { return dt == NMX_F32 || dt == NMX_U32 || dt == NMX_I32 ? 4 : 2; }
@@ -180,9 +179,6 @@ nmx_status_t Model::create(Ctx* c, const nmx_model_cfg& cfg, Model** out) {
       {&m->xn, size_t(T) * H * es},
       {&m->last_h, size_t(rows_logits) * H * es},
       {reinterpret_cast<void**>(&m->logits_f32), size_t(rows_logits) * V * 4},
-      {reinterpret_cast<void**>(&m->part_o), size_t(B) * cfg.n_heads * kMaxSplits * cfg.head_dim * 4},
-      {reinterpret_cast<void**>(&m->part_ml), size_t(B) * cfg.n_heads * kMaxSplits * 2 * 4},
-      {reinterpret_cast<void**>(&m->attn_counters), size_t(T) * cfg.n_kv_heads * 4},
       {reinterpret_cast<void**>(&m->am_val), size_t(32) * kArgmaxMaxGridPerSm * c->num_sms * 4},
       {reinterpret_cast<void**>(&m->am_idx), size_t(32) * kArgmaxMaxGridPerSm * c->num_sms * 4},
       {reinterpret_cast<void**>(&m->am_counter), 256},
@@ -265,8 +261,6 @@ Model::~Model() {
   for (auto& g : graphs) {
     if (g.second.exec) cudaGraphExecDestroy(g.second.exec);
   }
-  if (pers_ph) cudaFree(pers_ph);
-  if (pers_buf) cudaFree(pers_buf);
   if (pinned) cudaFreeHost(pinned);
   if (wsbase) cudaFree(wsbase);
   if (wbase) cudaFree(wbase);
@@ -583,8 +577,7 @@ nmx_status_t Model::run_layers_decode(KvPool* pool, int B) {
   Ctx* c = ctx;
   const nmx_model_cfg& cf = cfg;
   const int H = cf.hidden, F = cf.ffn, bits = cf.bits, gs = cf.group_size;
-  const int splits = std::max(1, std::min(kMaxSplits, (2 * c->num_sms + B * cf.n_kv_heads - 1) /
-                                                          (B * cf.n_kv_heads)));
+  const int splits = decode_attn_splits(c->num_sms, B, cf.n_kv_heads);
   NMX_TRY(embed_rows(c, embed, tok_ids, B, H, h));
   for (int l = 0; l < cf.n_layers; ++l) {
     LayerW& ly = layers[l];
@@ -595,7 +588,7 @@ nmx_status_t Model::run_layers_decode(KvPool* pool, int B) {
     at.k_cache = pool->k_layer(l); at.v_cache = pool->v_layer(l);
     at.block_tables = block_tables; at.max_blocks = kBlockCap;
     at.tok_seq = tok_seq; at.tok_pos = tok_pos; at.inv_freq = inv_freq;
-    at.out = attn; at.part_o = part_o; at.part_ml = part_ml; at.counters = attn_counters;
+    at.out = attn;
     at.T = B; at.Hq = cf.n_heads; at.Hkv = cf.n_kv_heads; at.D = cf.head_dim; at.BT = kBT;
     at.splits = splits; at.scale = 1.0f / std::sqrt(float(cf.head_dim));
     at.kv_static = true;
@@ -626,7 +619,6 @@ nmx_status_t Model::run_layers_prefill(KvPool* pool, int T) {
     at.k_cache = pool->k_layer(l); at.v_cache = pool->v_layer(l);
     at.block_tables = block_tables; at.max_blocks = kBlockCap;
     at.tok_seq = tok_seq; at.tok_pos = tok_pos; at.out = attn;
-    at.counters = attn_counters;
     at.T = T; at.Hq = cf.n_heads; at.Hkv = cf.n_kv_heads; at.D = cf.head_dim; at.BT = kBT;
     at.splits = 1; at.scale = 1.0f / std::sqrt(float(cf.head_dim));
     NMX_TRY(paged_prefill_attention(c, at, pf_items, n_pf_items));
@@ -789,18 +781,7 @@ nmx_status_t Model::forward(KvPool* pool, const nmx_seq_t* seqs, int n, nmx_out_
   const int rows = all ? T : n;
   NMX_CHECK(rows <= rows_logits, NMX_ERR_UNSUPPORTED, "forward: too many output rows for all-position mode");
   int out_rows = rows;
-  nmx_status_t pst = NMX_ERR_UNSUPPORTED;
-  if (decode && !all && !logits && persistent_ok(n)) {
-    pst = run_persistent(pool, 1, out_ids);
-    if (pst == NMX_ERR_UNSUPPORTED) {
-      persistent_unusable = true;
-      clear_error();
-    } else {
-      NMX_TRY(pst);
-    }
-  }
-  if (pst == NMX_OK) {
-  } else if (decode && !all && !logits) {
+  if (decode && !all && !logits) {
     NMX_TRY(run_decode_graph(pool, n));
   } else if (decode) {
     NMX_TRY(run_layers_decode(pool, n));
@@ -833,161 +814,6 @@ nmx_status_t Model::finish_step() {
   return NMX_OK;
 }
 
-// ------------------------------------------------- persistent batch-1 decode
-
-namespace {
-
-// CTAs of a GEMV phase: every SM, but no more than the tile groups (a tile
-// group then meets at most two CTAs) and at least 16 units per CTA (one per
-// warp)
-int phase_ctas(int num_sms, int n_tg, int K) {
-  const long long U = (long long)n_tg * (K / 128);
-  const long long g = std::min(std::min((long long)num_sms, (long long)n_tg), U / 16);
-  return int(g > 0 ? g : 0);
-}
-
-}  // namespace
-
-bool Model::persistent_ok(int B) const {
-  if (!persistent_enabled || persistent_unusable || B != 1 || (!weights_ready && !loaded_any)) return false;
-  if (comm) return false;  // the persistent schedule has no exchange phase
-  const nmx_model_cfg& cf = cfg;
-  const int rep = cf.n_kv_heads > 0 ? cf.n_heads / cf.n_kv_heads : 0;
-  if (!(cf.head_dim == 64 || cf.head_dim == 128) || rep < 1 || rep > 8 || cf.hidden % 8 != 0) return false;
-  if (cf.n_kv_heads > ctx->num_sms) return false;
-  const int sms = ctx->num_sms;
-  auto lin_ok = [&](const Lin& l, int n_out) { return l.dl && phase_ctas(sms, n_out / 16, l.K) >= 1; };
-  if (!lin_ok(lm, cf.vocab)) return false;
-  for (const auto& ly : layers)
-    if (!lin_ok(ly.qkv, Nqkv) || !lin_ok(ly.o, cf.hidden) || !lin_ok(ly.gu, cf.ffn) || !lin_ok(ly.down, cf.hidden))
-      return false;
-  return true;
-}
-
-nmx_status_t Model::persistent_prepare(KvPool* pool) {
-  if (pers_ph && pers_pool == pool) return NMX_OK;
-  Ctx* c = ctx;
-  const nmx_model_cfg& cf = cfg;
-  const int H = cf.hidden, F = cf.ffn, sms = c->num_sms, W = persist_warps();
-  std::vector<PPhase> ph;
-  int k_max = 0, lt_max = 1, red_slots = 1, ntg_max = 1;
-  auto gemv = [&](const Lin& l, int n_out, int epi, const void* x, const void* gamma, const void* bias, void* y,
-                  const void* res) {
-    PPhase p;
-    p.kind = PH_GEMV;
-    p.epi = epi;
-    p.tpt = epi == EPI_SILU ? 2 : 1;
-    p.n_tg = n_out / 16;
-    p.K = l.K;
-    p.G = phase_ctas(sms, p.n_tg, l.K);
-    const long long nb = l.K / 128, U = (long long)p.n_tg * nb;
-    const long long nmax = (U + p.G - 1) / p.G, per_warp = (U / p.G) / W;
-    p.lt_max = int(std::min<long long>(p.n_tg, (nmax + nb - 1) / nb + 1));
-    p.c_max = int(std::min<long long>(W, (nb + per_warp - 1) / per_warp + 1));
-    p.pair_off = epi == EPI_SILU ? (long long)p.n_tg * nb * 1152 : 0;
-    p.w = reinterpret_cast<const unsigned char*>(l.w);
-    p.x = static_cast<const half*>(x);
-    p.gamma = static_cast<const half*>(gamma);
-    p.bias = static_cast<const half*>(bias);
-    p.y = static_cast<half*>(y);
-    p.res = static_cast<const half*>(res);
-    k_max = std::max(k_max, p.K);
-    lt_max = std::max(lt_max, p.lt_max);
-    red_slots = std::max(red_slots, p.lt_max * p.c_max);
-    ntg_max = std::max(ntg_max, p.n_tg);
-    ph.push_back(p);
-  };
-  auto simple = [&](int kind, int layer) {
-    PPhase p;
-    p.kind = kind;
-    p.layer = layer;
-    ph.push_back(p);
-  };
-  simple(PH_EMBED, 0);
-  for (int l = 0; l < cf.n_layers; ++l) {
-    const LayerW& ly = layers[l];
-    gemv(ly.qkv, Nqkv, EPI_STORE, h, ly.attn_norm, ly.qkv_bias, qkv, nullptr);
-    simple(PH_ATTN, l);
-    simple(PH_COMBINE, l);
-    gemv(ly.o, H, EPI_RESID, attn, nullptr, nullptr, h, h);
-    gemv(ly.gu, F, EPI_SILU, h, ly.mlp_norm, nullptr, act, nullptr);
-    gemv(ly.down, H, EPI_RESID, act, nullptr, nullptr, h, h);
-  }
-  gemv(lm, cf.vocab, EPI_ARGMAX, h, final_norm, nullptr, nullptr, nullptr);
-  simple(PH_ADVANCE, 0);
-
-  const int rep = cf.n_heads / cf.n_kv_heads;
-  const int S = std::max(1, std::min(32, sms / cf.n_kv_heads));  // key splits: one item per CTA
-  const size_t items = size_t(cf.n_kv_heads) * S;
-  const size_t b_part_o = align_up(items * rep * cf.head_dim * 4, 256);
-  const size_t b_part_ml = align_up(items * rep * 8, 256);
-  const size_t b_flags = align_up(size_t(ntg_max) * 4, 256);
-  const size_t b_hand = align_up(size_t(ntg_max) * 32 * 4, 256);
-  const size_t b_best = align_up(size_t(sms) * 8, 256);
-  const size_t b_bar = 256;
-  const size_t total = b_part_o + b_part_ml + b_flags + b_hand + b_best + b_bar;
-  if (pers_ph) cudaFree(pers_ph);
-  if (pers_buf) cudaFree(pers_buf);
-  pers_ph = nullptr;
-  pers_buf = nullptr;
-  NMX_TRY(alloc_dev(reinterpret_cast<void**>(&pers_ph), ph.size() * sizeof(PPhase)));
-  NMX_TRY(alloc_dev(reinterpret_cast<void**>(&pers_buf), total));
-  NMX_CUDA_OK(cudaMemcpyAsync(pers_ph, ph.data(), ph.size() * sizeof(PPhase), cudaMemcpyHostToDevice, c->stream));
-  NMX_CUDA_OK(cudaMemsetAsync(pers_buf, 0, total, c->stream));
-  NMX_CUDA_OK(cudaStreamSynchronize(c->stream));
-
-  PersistArgs A{};
-  A.ph = pers_ph;
-  A.n_ph = int(ph.size());
-  A.tok_ids = tok_ids;
-  A.tok_pos = tok_pos;
-  A.hist = hist;
-  A.hist_cap = kHistCap;
-  A.step = step;
-  A.table = block_tables;
-  A.kv_base = pool->base;
-  A.kv_layer_stride = pool->layer_stride;
-  A.Hq = cf.n_heads;
-  A.Hkv = cf.n_kv_heads;
-  A.D = cf.head_dim;
-  A.S = S;
-  A.scale = 1.0f / std::sqrt(float(cf.head_dim));
-  A.inv_freq = inv_freq;
-  A.eps = cf.rms_eps;
-  A.embed = static_cast<const half*>(embed);
-  A.H = H;
-  A.h = static_cast<half*>(h);
-  A.qkv = static_cast<const half*>(qkv);
-  A.attn = static_cast<half*>(attn);
-  char* b = pers_buf;
-  A.part_o = reinterpret_cast<float*>(b);
-  b += b_part_o;
-  A.part_ml = reinterpret_cast<float*>(b);
-  b += b_part_ml;
-  A.flags = reinterpret_cast<unsigned*>(b);
-  b += b_flags;
-  A.hand = reinterpret_cast<float*>(b);
-  b += b_hand;
-  A.best = reinterpret_cast<unsigned long long*>(b);
-  b += b_best;
-  A.bar = reinterpret_cast<unsigned*>(b);
-  A.err = c->dev_err;
-  NMX_TRY(persist_layout(k_max, red_slots, lt_max, &A));
-  pers_smem = persist_smem_bytes(k_max, red_slots, lt_max, cf.head_dim);
-  pers_args = A;
-  pers_pool = pool;
-  return NMX_OK;
-}
-
-// the batch-1 step(s) from the uploaded token / position / block table
-nmx_status_t Model::run_persistent(KvPool* pool, int steps, int* out_id) {
-  NMX_TRY(persistent_prepare(pool));
-  PersistArgs A = pers_args;
-  A.steps = steps;
-  A.out_id = out_id;
-  return persist_launch(ctx, A, pers_smem);
-}
-
 nmx_status_t Model::decode_greedy(KvPool* pool, const int32_t* first, const int32_t* start,
                                   const int32_t* tables, int max_blocks_in, int n, int steps,
                                   int32_t* out_host) {
@@ -1017,20 +843,6 @@ nmx_status_t Model::decode_greedy(KvPool* pool, const int32_t* first, const int3
   for (int i = 0; i < n; ++i)
     NMX_CUDA_OK(cudaMemcpy2DAsync(block_tables + size_t(i) * kBlockCap, 4, tables + size_t(i) * max_blocks_in, 4,
                                   4, max_blocks_in, cudaMemcpyHostToDevice, c->stream));
-  if (persistent_ok(n) && steps > 0) {
-    // one cooperative launch runs every step
-    NMX_CUDA_OK(cudaMemcpyAsync(tok_pos, ps, size_t(n) * 4, cudaMemcpyHostToDevice, c->stream));
-    NMX_CUDA_OK(cudaMemcpyAsync(step, zero, 4, cudaMemcpyHostToDevice, c->stream));
-    const nmx_status_t st = run_persistent(pool, steps, nullptr);
-    if (st == NMX_OK) {
-      if (out_host)
-        NMX_CUDA_OK(cudaMemcpyAsync(out_host, hist, size_t(steps) * n * 4, cudaMemcpyDeviceToHost, c->stream));
-      return finish_step();
-    }
-    if (st != NMX_ERR_UNSUPPORTED) return st;
-    persistent_unusable = true;  // this device cannot run it: the graph below does the steps
-    clear_error();
-  }
   // graph capture happens outside the timed steps: build it first if needed
   auto key = std::make_pair(n, static_cast<const void*>(pool));
   if (graphs.find(key) == graphs.end()) {

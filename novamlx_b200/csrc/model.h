@@ -59,8 +59,6 @@ struct Model {
   void *h = nullptr, *qkv = nullptr, *q_roped = nullptr, *attn = nullptr, *act = nullptr, *last_h = nullptr;
   void* xn = nullptr;  // RMSNorm output for the tensor-core GEMM (prefill)
   float* logits_f32 = nullptr;
-  float *part_o = nullptr, *part_ml = nullptr;
-  unsigned* attn_counters = nullptr;
   float* am_val = nullptr;
   int* am_idx = nullptr;
   unsigned* am_counter = nullptr;
@@ -115,22 +113,11 @@ struct Model {
   nmx_status_t upload_batch(const nmx_seq_t* seqs, int n, int* T_out, bool* decode_out);
   nmx_status_t forward(KvPool* pool, const nmx_seq_t* seqs, int n, nmx_out_mode_t mode, void* out_host);
   nmx_status_t finish_step();
-  // persistent batch-1 decode (decode_persistent.cu)
   // tensor parallelism: this rank's shard of every linear; o/down partials
   // are exchanged and summed (with the residual) through the communicator
   Comm* comm = nullptr;
   nmx_comm_s* comm_handle = nullptr;
   bool fused_exchange = false;  // decode batches: the GEMM epilogue does the exchange (nmx_model_set_exchange_fusion)
-  bool persistent_enabled = false;  // opt-in: the per-layer graph is faster today
-  bool persistent_unusable = false;  // the device refused the launch (cooperative / shared memory)
-  PPhase* pers_ph = nullptr;
-  char* pers_buf = nullptr;
-  const void* pers_pool = nullptr;
-  PersistArgs pers_args{};
-  size_t pers_smem = 0;
-  bool persistent_ok(int B) const;
-  nmx_status_t persistent_prepare(KvPool* pool);
-  nmx_status_t run_persistent(KvPool* pool, int steps, int* out_id);
 
   nmx_status_t decode_greedy(KvPool* pool, const int32_t* first, const int32_t* start, const int32_t* tables,
                              int max_blocks, int n, int steps, int32_t* out_host);

@@ -14,7 +14,6 @@
 namespace nmx {
 namespace tc {
 
-constexpr unsigned kGSpin = 1u << 24;  // polls before a wait gives up
 constexpr int kRecG = 1152;            // bytes of one decode record (16 rows x 128 k)
 
 __device__ __forceinline__ unsigned sa_(const void* p) { return static_cast<unsigned>(__cvta_generic_to_shared(p)); }
@@ -35,9 +34,10 @@ __device__ __forceinline__ bool mbar_try(unsigned a, unsigned parity) {
                : "memory");
   return ok != 0;
 }
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity) {
+// bounded: false after `lim` polls (the context's wait limit)
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity, unsigned lim) {
   const unsigned a = sa_(b);
-  for (unsigned it = 0; it < kGSpin; ++it)
+  for (unsigned it = 0; it < lim; ++it)
     if (mbar_try(a, parity)) return true;
   return false;
 }

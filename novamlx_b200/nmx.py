@@ -77,6 +77,7 @@ _proto("nmx_ctx_set_stream", _i, _vp, _vp)
 _proto("nmx_ctx_stream", _vp, _vp)
 _proto("nmx_ctx_synchronize", _i, _vp)
 _proto("nmx_ctx_kernel_launches", _u64, _vp)
+_proto("nmx_ctx_set_wait_limit", _i, _vp, C.c_uint32)
 _proto("nmx_op_qmatmul", _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp)
 _proto("nmx_op_pack_records", _i, _vp, _vp, _vp, _vp, _i, _i, _vp)
 _proto("nmx_op_qmatmul_records", _i, _vp, _vp, _vp, _i, _i, _i, _vp)
@@ -96,7 +97,6 @@ _proto("nmx_model_load_tensor", _i, _vp, C.c_char_p, _vp, _i, C.POINTER(C.c_int6
 _proto("nmx_model_get_tensor", _i, _vp, C.c_char_p, _vp, _sz)
 _proto("nmx_model_weight_bytes", _u64, _vp)
 _proto("nmx_model_step_weight_bytes", _u64, _vp)
-_proto("nmx_model_set_persistent_decode", _i, _vp, _i)
 _proto("nmx_kv_pool_create", _i, _vp, _i, _i, C.POINTER(_vp))
 _proto("nmx_kv_pool_destroy", _i, _vp)
 _proto("nmx_kv_copy_blocks", _i, _vp, _ip, _ip, _i)
@@ -267,6 +267,11 @@ class Context:
 
     def synchronize(self):
         check(lib.nmx_ctx_synchronize(self.h))
+
+    def set_wait_limit(self, polls: int = 0):
+        """Polls a device-side wait makes before giving up with
+        NMX_ERR_TIMEOUT (0: the default, 2^24)."""
+        check(lib.nmx_ctx_set_wait_limit(self.h, int(polls)))
 
     @property
     def launches(self) -> int:
@@ -560,10 +565,6 @@ class Model:
     @property
     def step_weight_bytes(self) -> int:
         return int(lib.nmx_model_step_weight_bytes(self.h))
-
-    def set_persistent_decode(self, enable: bool) -> None:
-        """Batch-1 decode as one persistent launch, or (default) a graph of per-layer kernels."""
-        check(lib.nmx_model_set_persistent_decode(self.h, 1 if enable else 0))
 
     @property
     def kv_bytes_per_token(self) -> int:

@@ -7,6 +7,8 @@ import numpy as np
 import pytest
 
 from oracle import oracle as O
+from parity import check_id
+from parity import check_logits as _check_logits_rule
 
 pytestmark = pytest.mark.gpu
 
@@ -41,9 +43,8 @@ def build(ctx, name, seed=1, max_batch=8, max_tokens=512):
 
 
 def check_logits(got, ref):
-    for g, r in zip(np.atleast_2d(got), np.atleast_2d(ref)):
-        assert O.cosine(g, r) >= 0.999
-        assert O.max_rel_err(g, r) <= 2e-2
+    """Cosine and normwise error of every row; the largest abs logit error."""
+    return _check_logits_rule(got, ref)
 
 
 @pytest.mark.parametrize("name", ["llama", "qwen", "llama8"])
@@ -147,18 +148,23 @@ def test_decode_greedy_loop_equals_host_loop(ctx):
                         nmx.OUT_ARGMAX_LAST)
         host.append(cur.copy())
     assert np.array_equal(dev_ids, np.stack(host))
-    # and the oracle, teacher-forced on the GPU's ids, agrees on most steps
-    agree = 0
+    # and the oracle, teacher-forced on the GPU's ids: logits within the bars
+    # at every step, and every id the oracle's argmax wherever that is
+    # determined (top-2 gap above twice the measured logit error)
+    m.forward(pool, [dict(tokens=p, start_pos=0, block_table=t) for p, t in zip(prompts, tables)],
+              nmx.OUT_ARGMAX_LAST)
     for i in range(B):
         c = om.new_cache(64)
         r = om.forward(c, prompts[i], 0)
-        agree += int(np.argmax(r[0]) == first[i])
+        g = m.forward(pool, [dict(tokens=prompts[i], start_pos=0, block_table=tables[i])], nmx.OUT_LOGITS_LAST)
+        check_id(first[i], r, check_logits(g, r))
         tok = first[i]
         for s in range(S):
             r = om.forward(c, [tok], P + s)
-            agree += int(np.argmax(r[0]) == dev_ids[s, i])
+            g = m.forward(pool, [dict(tokens=[tok], start_pos=P + s, block_table=tables[i])], nmx.OUT_LOGITS_LAST)
+            assert dev_ids[s, i] == int(np.argmax(g[0]))
+            check_id(dev_ids[s, i], r, check_logits(g, r))
             tok = dev_ids[s, i]
-    assert agree >= int(0.9 * B * (S + 1))
 
 
 def test_forward_rejects_bad_inputs(ctx):
@@ -223,43 +229,6 @@ def test_wide_layer_matches_oracle(ctx):
         ids = m.forward(pool, [dict(tokens=[tok], start_pos=pos, block_table=table)], nmx.OUT_ARGMAX_LAST)
         assert ids[0] == int(np.argmax(g[0]))
         pos += 1
-
-
-@pytest.mark.parametrize("name", ["llama", "qwen"])
-def test_persistent_decode_matches_graph_decode(ctx, name):
-    """Batch-1 greedy decode as one persistent launch equals the per-layer
-    kernel graph (same pages, same ids), and its first step's id is the
-    argmax of the oracle's logits teacher-forced on the same tokens."""
-    from novamlx_b200 import nmx
-    m, om, cfg = build(ctx, name)
-    pool = nmx.KVPool(m, 40)
-    rng = np.random.default_rng(21)
-    P, S = 37, 24
-    prompt = rng.integers(0, cfg.vocab, P)
-    table = rng.permutation(40)[:8].astype(np.int32)
-    runs = []
-    for persistent in (True, False):
-        m.set_persistent_decode(persistent)
-        first = m.forward(pool, [dict(tokens=prompt, start_pos=0, block_table=table)], nmx.OUT_ARGMAX_LAST)
-        n0 = ctx.launches
-        runs.append((first.copy(), m.decode_greedy(pool, first, [P], table[None], S)))
-        if persistent:
-            assert ctx.launches - n0 == 1  # every step in one launch
-    m.set_persistent_decode(True)
-    assert np.array_equal(runs[0][0], runs[1][0])
-    assert np.array_equal(runs[0][1], runs[1][1])
-    # the host-facing batch-1 decode step (persistent, steps = 1) agrees too
-    m.forward(pool, [dict(tokens=prompt, start_pos=0, block_table=table)], nmx.OUT_ARGMAX_LAST)
-    cur = int(runs[0][0][0])
-    for s in range(4):
-        cur = int(m.forward(pool, [dict(tokens=[cur], start_pos=P + s, block_table=table)], nmx.OUT_ARGMAX_LAST)[0])
-        assert cur == runs[0][1][s, 0]
-    c = om.new_cache(64)
-    om.forward(c, prompt, 0)
-    r = om.forward(c, [int(runs[0][0][0])], P)
-    top2 = np.sort(r[0])[-2:]
-    if top2[1] - top2[0] > 1e-2:  # no near-tie: the id is determined
-        assert int(np.argmax(r[0])) == runs[0][1][0, 0]
 
 
 @pytest.mark.parametrize("name", ["llama", "qwen"])

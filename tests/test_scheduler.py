@@ -91,21 +91,30 @@ def _run(sched, ids, max_steps=2000):
     raise AssertionError("scheduler did not drain")
 
 
-def _check_against_oracle(om, prompt, out):
-    """Teacher-force the scheduler's ids through the oracle: each id is the
-    oracle's argmax or within a near-tie of it; most are the argmax."""
-    from oracle import oracle as O
-    cache = om.new_cache(len(prompt) + len(out) + 16)
-    r = om.forward(cache, prompt, 0)[0]
-    exact = 0
+def _check_against_oracle(m, om, prompt, out):
+    """Teacher-force the scheduler's ids through the oracle and through a
+    batch-1 GPU forward of the same model: the GPU logits are within the bars
+    at every step, and each id is the oracle's argmax wherever that is
+    determined. The scheduler computed its ids inside batches (other rows,
+    other summation orders), so the band is twice the batch-1 error measured
+    at that step. Returns the number of determined ids."""
+    from novamlx_b200 import nmx
+    from parity import check_id, check_logits
+    n = len(prompt) + len(out) + 16
+    pool = nmx.KVPool(m, (n + 15) // 16)
+    table = np.arange((n + 15) // 16, dtype=np.int32)
+    cache = om.new_cache(n)
+    r = om.forward(cache, prompt, 0)
+    g = m.forward(pool, [dict(tokens=prompt, start_pos=0, block_table=table)], nmx.OUT_LOGITS_LAST)
+    determined = 0
     pos = len(prompt)
     for tok in out:
-        tol = 2e-2 * float(np.max(np.abs(r)))
-        assert r[tok] >= r.max() - tol, (tok, int(np.argmax(r)), float(r[tok]), float(r.max()))
-        exact += int(tok == int(np.argmax(r)))
-        r = om.forward(cache, [int(tok)], pos)[0]
+        determined += int(check_id(int(tok), r, 2.0 * check_logits(g, r)))
+        r = om.forward(cache, [int(tok)], pos)
+        g = m.forward(pool, [dict(tokens=[int(tok)], start_pos=pos, block_table=table)], nmx.OUT_LOGITS_LAST)
         pos += 1
-    return exact
+    pool.close()
+    return determined
 
 
 @pytest.mark.gpu
@@ -124,13 +133,10 @@ def test_scheduler_matches_oracle_with_shared_prefix(nmx):
     ids = [sched.submit(p, n) for p, n in zip(prompts, max_new)]
     _run(sched, ids)
     st = sched.stats()
-    exact = total = 0
     for rid, p, n in zip(ids, prompts, max_new):
         out, state = sched.poll(rid)
         assert state == nmx.REQ_DONE and len(out) == n
-        exact += _check_against_oracle(om, p, out)
-        total += n
-    assert exact >= int(0.9 * total)
+        _check_against_oracle(m, om, p, out)
     # the 48-token prefix (three full pages) was computed once and reused twice
     assert st["prefix_hit_tokens"] == 2 * 48
     assert st["finished"] == len(ids) and st["running"] == 0 and st["waiting"] == 0
@@ -165,7 +171,7 @@ def test_scheduler_shares_prefix_pages_while_running(nmx):
     for rid, p in zip(ids, prompts):
         out, _ = sched.poll(rid)
         assert len(out) == 16
-        _check_against_oracle(om, p, out)
+        _check_against_oracle(m, om, p, out)
     sched.close()
 
 
@@ -192,7 +198,7 @@ def test_scheduler_preempts_newest_on_page_exhaustion(nmx):
         if s == nmx.REQ_DONE:
             out, _ = sched.poll(rid)
             assert len(out) == 24
-            _check_against_oracle(om, p, out)
+            _check_against_oracle(m, om, p, out)
     again = [sched.submit(p, 24) for p, s in zip(prompts, states) if s == nmx.REQ_PREEMPTED]
     _run(sched, again)
     for rid in again:

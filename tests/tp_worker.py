@@ -1,8 +1,10 @@
 """One rank of the tensor-parallel parity check (test infrastructure; run
 under torch.distributed.run by tests/test_tp.py). Every rank loads its shard
 of the same tiny model, joins the communicator, and runs a ragged prefill, a
-batched decode step and a device greedy loop; rank 0 also runs the unsharded
-model on its GPU and writes both results to the output file."""
+device greedy loop, the same steps teacher-forced with logits, and a
+12-sequence batch through the decode-batch GEMM (with and without the
+exchange fused into its epilogue). Each rank writes its results; the test
+compares them with the oracle and with each other."""
 import argparse
 import os
 import sys
@@ -11,6 +13,8 @@ import numpy as np
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
+GREEDY_STEPS = 6
+
 
 def tiny(name):
     llama = dict(vocab=1024, hidden=512, n_layers=2, n_heads=8, n_kv_heads=2, head_dim=64, ffn=1024,
@@ -18,30 +22,52 @@ def tiny(name):
                  rope_original_max_pos=64, rms_eps=1e-5)
     qwen = dict(vocab=1024, hidden=512, n_layers=2, n_heads=4, n_kv_heads=2, head_dim=128, ffn=1536,
                 qkv_bias=True, rope_theta=1e6, rms_eps=1e-6)
-    return {"llama": llama, "qwen": qwen}[name]
+    # eight kv heads: shard over 2, 4 and 8 ranks (one kv head per rank at 8)
+    llama8kv = dict(llama, n_heads=16, n_kv_heads=8, ffn=2048)
+    # the Qwen2.5-32B head layout (40 q heads / 8 kv heads of 128: 5 q heads
+    # per kv head, 5/1 per rank at 8 ranks)
+    qwen8kv = dict(qwen, n_heads=40, n_kv_heads=8, ffn=2048)
+    return {"llama": llama, "qwen": qwen, "llama8kv": llama8kv, "qwen8kv": qwen8kv}[name]
 
 
-def run(nmx, m, pool, rng_seed, cfg):
-    rng = np.random.default_rng(rng_seed)
+def prompts_of(cfg, seed):
+    rng = np.random.default_rng(seed)
     lens = [3, 40, 17, 70]
     prompts = [rng.integers(0, cfg.vocab, n) for n in lens]
     tables = [np.arange(8 * i + 1, 8 * i + 9, dtype=np.int32) for i in range(4)]
+    return lens, prompts, tables
+
+
+def run(nmx, m, pool, cfg, seed):
+    lens, prompts, tables = prompts_of(cfg, seed)
     logits = m.forward(pool, [dict(tokens=p, start_pos=0, block_table=t) for p, t in zip(prompts, tables)],
                        nmx.OUT_LOGITS_LAST)
     first = m.forward(pool, [dict(tokens=p, start_pos=0, block_table=t) for p, t in zip(prompts, tables)])
-    ids = m.decode_greedy(pool, first, lens, np.stack(tables), 6)
-    return logits, first, ids
+    ids = m.decode_greedy(pool, first, lens, np.stack(tables), GREEDY_STEPS)
+    # the same steps teacher-forced on the greedy ids, with logits
+    step_logits = []
+    cur = first.copy()
+    for s in range(GREEDY_STEPS):
+        step_logits.append(m.forward(pool, [dict(tokens=[int(cur[i])], start_pos=lens[i] + s, block_table=tables[i])
+                                            for i in range(4)], nmx.OUT_LOGITS_LAST))
+        cur = ids[s]
+    return logits, first, ids, np.stack(step_logits)
 
 
-def run_batch(nmx, m, pool, rng_seed, cfg):
+def batch_inputs(cfg, seed):
+    rng = np.random.default_rng(seed)
+    prompts = [rng.integers(0, cfg.vocab, 8) for _ in range(12)]
+    toks = rng.integers(0, cfg.vocab, 12)
+    return prompts, toks
+
+
+def run_batch(nmx, m, pool, cfg, seed):
     """12 short prompts prefilled together (96 rows) and one 12-row decode
     step: the decode-batch GEMM path, whose epilogue can do the exchange"""
-    rng = np.random.default_rng(rng_seed)
-    prompts = [rng.integers(0, cfg.vocab, 8) for _ in range(12)]
+    prompts, toks = batch_inputs(cfg, seed)
     tables = [np.array([100 + i], np.int32) for i in range(12)]
     pre = m.forward(pool, [dict(tokens=p, start_pos=0, block_table=t) for p, t in zip(prompts, tables)],
                     nmx.OUT_LOGITS_LAST)
-    toks = rng.integers(0, cfg.vocab, 12)
     dec = m.forward(pool, [dict(tokens=[int(x)], start_pos=8, block_table=t) for x, t in zip(toks, tables)],
                     nmx.OUT_LOGITS_LAST)
     return np.concatenate([pre, dec])
@@ -83,25 +109,16 @@ def main():
     expect = (1 + base * sum(range(1, world + 1))).half()
     op_ok = bool(torch.equal(out, expect))
 
-    tp_logits, tp_first, tp_ids = run(nmx, m, pool, 11, full_cfg)
+    tp_logits, tp_first, tp_ids, tp_step_logits = run(nmx, m, pool, full_cfg, 11)
     m.set_exchange_fusion(True)
-    tp_batch = run_batch(nmx, m, pool, 12, full_cfg)       # exchange fused into the GEMM
+    tp_batch = run_batch(nmx, m, pool, full_cfg, 12)       # exchange fused into the GEMM
     m.set_exchange_fusion(False)
-    tp_batch_sep = run_batch(nmx, m, pool, 12, full_cfg)   # GEMM, then the exchange kernel
+    tp_batch_sep = run_batch(nmx, m, pool, full_cfg, 12)   # GEMM, then the exchange kernel
     dist.barrier()
     m.set_comm(None)
     comm.close()
-    result = dict(op_ok=np.array(op_ok), tp_logits=tp_logits, tp_first=tp_first, tp_ids=tp_ids,
-                  tp_batch=tp_batch, tp_batch_sep=tp_batch_sep)
-    if rank == 0:
-        fm = nmx.Model(ctx, full_cfg)
-        for k, v in tensors.items():
-            fm.load_tensor(k, v.view(np.float16) if v.dtype == np.uint16 else v)
-        fpool = nmx.KVPool(fm, 120)
-        f_logits, f_first, f_ids = run(nmx, fm, fpool, 11, full_cfg)
-        f_batch = run_batch(nmx, fm, fpool, 12, full_cfg)
-        result.update(full_logits=f_logits, full_first=f_first, full_ids=f_ids, full_batch=f_batch)
-    np.savez(f"{a.out}.rank{rank}.npz", **result)
+    np.savez(f"{a.out}.rank{rank}.npz", op_ok=np.array(op_ok), tp_logits=tp_logits, tp_first=tp_first,
+             tp_ids=tp_ids, tp_step_logits=tp_step_logits, tp_batch=tp_batch, tp_batch_sep=tp_batch_sep)
     dist.barrier()
     dist.destroy_process_group()
 
