@@ -308,6 +308,10 @@ NMX_API nmx_status_t nmx_kv_write_blocks(nmx_kv_pool_t pool, const int32_t* ids,
 /* Device pointers of layer `layer`'s K and V pages (for op-level tests). */
 NMX_API nmx_status_t nmx_kv_pool_layer_ptrs(nmx_kv_pool_t pool, int layer, void** k, void** v);
 NMX_API int nmx_kv_pool_num_blocks(nmx_kv_pool_t pool);
+/* Fill every page of every layer (K and V) with seeded N(0, std) values: a
+ * KV cache of a given context without running its prefill (benchmark and
+ * test set-up). No counterpart in the reference. */
+NMX_API nmx_status_t nmx_kv_pool_fill_random(nmx_kv_pool_t pool, uint64_t seed, float std);
 /* KV bytes one token occupies over all layers: 2 * layers * Hkv * head_dim * 2,
  * the engine's kvMemoryBytesPerToken (Sources/NovaMLXEngine/MLXEngine.swift:833). */
 NMX_API uint64_t nmx_kv_bytes_per_token(nmx_model_t model);

@@ -518,6 +518,17 @@ NMX_API nmx_status_t nmx_kv_pool_layer_ptrs(nmx_kv_pool_t pool, int layer, void*
 
 NMX_API int nmx_kv_pool_num_blocks(nmx_kv_pool_t pool) { return pool ? pool->p->num_blocks : 0; }
 
+NMX_API nmx_status_t nmx_kv_pool_fill_random(nmx_kv_pool_t pool, uint64_t seed, float std) {
+  API_BEGIN;
+  REQUIRE(pool, "pool");
+  KvPool* p = pool->p;
+  Ctx* c = p->model->ctx;
+  const size_t halves = p->layer_stride * size_t(p->model->cfg.n_layers) / 2;
+  NMX_TRY(random_fill(c, seed, 0x6b76ull, std, 0.f, halves, NMX_F16, p->base));
+  NMX_CUDA_OK(cudaStreamSynchronize(c->stream));
+  return NMX_OK;
+}
+
 NMX_API uint64_t nmx_kv_bytes_per_token(nmx_model_t model) {
   if (!model) return 0;
   const auto& c = model->m->cfg;

@@ -104,6 +104,7 @@ _proto("nmx_kv_read_blocks", _i, _vp, _ip, _i, _vp)
 _proto("nmx_kv_write_blocks", _i, _vp, _ip, _i, _vp)
 _proto("nmx_kv_pool_layer_ptrs", _i, _vp, _i, C.POINTER(_vp), C.POINTER(_vp))
 _proto("nmx_kv_pool_num_blocks", _i, _vp)
+_proto("nmx_kv_pool_fill_random", _i, _vp, _u64, C.c_float)
 _proto("nmx_kv_bytes_per_token", _u64, _vp)
 _proto("nmx_forward", _i, _vp, _vp, C.POINTER(Seq), _i, _i, _vp)
 _proto("nmx_decode_greedy", _i, _vp, _vp, _ip, _ip, _ip, _i, _i, _i, _ip)
@@ -616,6 +617,10 @@ class KVPool:
         self.model = model
         self.num_blocks = num_blocks
         self.block_tokens = block_tokens
+
+    def fill_random(self, seed: int = 0, std: float = 1.0):
+        """Every page of every layer N(0, std): a cache of a given context without its prefill."""
+        check(lib.nmx_kv_pool_fill_random(self.h, seed, std))
 
     def layer_ptrs(self, layer: int):
         k, v = _vp(), _vp()
