@@ -245,11 +245,14 @@ def test_qmatmul_rejects_bad_shapes(env):
         ctx.quantized_matmul(x[:, :64].contiguous(), w[:, :8].contiguous(), s, s, group_size=64, bits=3)
 
 
-def test_rmsnorm(env):
+@pytest.mark.parametrize("M,H", [(5, 4096), (32, 5120), (3, 8192), (2, 24576), (4, 1000)])
+def test_rmsnorm(env, M, H):
+    """Vectorised rows (H % 8 == 0: one or two 16-byte chunks per thread)
+    and the scalar fallback (H = 1000)."""
     torch, nmx, ctx = env
     rng = np.random.default_rng(2)
-    x = O.f32_to_f16bits(rng.standard_normal((5, 4096), dtype=np.float32) * 3)
-    g = O.f32_to_f16bits(1 + 0.1 * rng.standard_normal(4096, dtype=np.float32))
+    x = O.f32_to_f16bits(rng.standard_normal((M, H), dtype=np.float32) * 3)
+    g = O.f32_to_f16bits(1 + 0.1 * rng.standard_normal(H, dtype=np.float32))
     y = host16(ctx.rms_norm(u16(torch, x), u16(torch, g), 1e-5))
     ref = O.rmsnorm(x, g, 1e-5)
     d = np.abs(O.f16bits_to_f32(y) - O.f16bits_to_f32(ref))
