@@ -19,6 +19,7 @@
 #include <algorithm>
 #include <map>
 #include <mutex>
+#include <vector>
 
 #include "attn_common.cuh"
 #include "common.cuh"
@@ -219,14 +220,24 @@ nmx_status_t launch_prefill(Ctx* c, const AttnArgs& a, const int2* items, int n_
 
 }  // namespace
 
-int prefill_items(const int32_t* row_seq, int T, int2* items_host) {
+int prefill_items(const int32_t* row_seq, int T, int D, int rep, int2* items_host, int* n_tc) {
+  const bool tc = prefill_tc_supported(D, rep);
+  const int qp = tc ? 128 / rep : kPQB;
+  std::vector<int2> small;
   int n = 0;
   for (int r = 0; r < T;) {
     int e = r + 1;
-    while (e < T && e - r < kPQB && row_seq[e] == row_seq[r]) ++e;
-    items_host[n++] = make_int2(r, e - r);
+    while (e < T && e - r < qp && row_seq[e] == row_seq[r]) ++e;
+    const int nr = e - r;
+    if (tc && !(nr <= kPQB && nr * rep < 64)) {
+      items_host[n++] = make_int2(r, nr);
+    } else {
+      for (int s = r; s < e; s += kPQB) small.push_back(make_int2(s, std::min(kPQB, e - s)));
+    }
     r = e;
   }
+  *n_tc = n;
+  for (const int2& it : small) items_host[n++] = it;
   return n;
 }
 
@@ -235,6 +246,11 @@ nmx_status_t paged_prefill_attention(Ctx* c, const AttnArgs& a, const int2* item
   NMX_CHECK(a.Hkv > 0 && a.Hq % a.Hkv == 0 && a.Hq / a.Hkv <= kPMaxRep, NMX_ERR_UNSUPPORTED,
             "prefill attention: q heads per kv head must be <= 8");
   if (n_items == 0) return NMX_OK;
+  const int n_tc = std::min(a.prefill_tc_items, n_items);
+  if (n_tc > 0) NMX_TRY(paged_prefill_attention_tc(c, a, items, n_tc));
+  if (n_tc == n_items) return NMX_OK;
+  items += n_tc;
+  n_items -= n_tc;
   if (a.D == 128) return launch_prefill<128>(c, a, items, n_items);
   if (a.D == 64) return launch_prefill<64>(c, a, items, n_items);
   NMX_CHECK(false, NMX_ERR_UNSUPPORTED, "prefill attention: head_dim must be 64 or 128");

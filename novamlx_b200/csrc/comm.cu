@@ -14,9 +14,10 @@
 // wrote this rank's partial into its region with the store epilogue):
 //   1. after the programmatic-launch wait (the partial is complete), CTA 0
 //      publishes epoch e = old + 1 to every peer's flag slot for this rank
-//      (system-scope release store over NVLink);
-//   2. every CTA waits (bounded, acquire) until all peers' flags in its own
-//      arena reach e;
+//      (one system-scope fence, then plain stores over NVLink: a release
+//      store per peer serialised a fence per peer);
+//   2. every CTA waits (bounded) until all peers' flags in its own arena
+//      reach e, then one system-scope fence orders its reads after them;
 //   3. each thread sums the partials of ranks 0..t-1 (peer loads, fixed rank
 //      order, f32) plus the residual and writes the new hidden row — the
 //      same bits on every rank;
@@ -55,14 +56,15 @@ struct ARArgs {
   unsigned* err;
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(unsigned* p, unsigned v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+__device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned* p) {
   unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 __global__ void __launch_bounds__(kARThreads) allreduce_resid_kernel(ARArgs a) {
   __shared__ unsigned s_e;
@@ -72,14 +74,16 @@ __global__ void __launch_bounds__(kARThreads) allreduce_resid_kernel(ARArgs a) {
     const unsigned e = *reinterpret_cast<volatile unsigned*>(a.epoch) + 1u;
     s_e = e;
     if (blockIdx.x == 0) {
-      __threadfence_system();
-      for (int q = 0; q < a.world; ++q) st_release_sys(a.peer_flag[q], e);
+      // one system-scope fence orders the partial (and everything this rank
+      // wrote before) ahead of the flags, then plain stores publish them
+      fence_acq_rel_sys();
+      for (int q = 0; q < a.world; ++q) st_relaxed_sys(a.peer_flag[q], e);
     }
     int ok = 1;
     const unsigned lim = wait_polls(a.err);
     for (int q = 0; q < a.world && ok; ++q) {
       unsigned it = 0;
-      while ((int)(ld_acquire_sys(a.my_flags + q) - e) < 0) {
+      while ((int)(ld_relaxed_sys(a.my_flags + q) - e) < 0) {
         if (++it >= lim) {
           ok = 0;
           atomicOr(a.err, kErrPeerWait);
@@ -87,6 +91,8 @@ __global__ void __launch_bounds__(kARThreads) allreduce_resid_kernel(ARArgs a) {
         }
       }
     }
+    // every flag seen: the peers' partials written before them are visible
+    fence_acq_rel_sys();
     s_ok = ok;
   }
   __syncthreads();
@@ -96,12 +102,18 @@ __global__ void __launch_bounds__(kARThreads) allreduce_resid_kernel(ARArgs a) {
     const long total = (long)a.rows * c8;
     for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
       const int r = int(i / c8), c = int(i % c8) * 8;
+      // all ranks' 16-byte pieces in flight at once, then the sum in rank order
+      uint4 v[kMaxRanks];
+#pragma unroll
+      for (int q = 0; q < kMaxRanks; ++q)
+        if (q < a.world) v[q] = __ldcv(reinterpret_cast<const uint4*>(a.part[q] + (long)r * a.cols + c));
       float acc[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-      for (int q = 0; q < a.world; ++q) {
-        const uint4 v = __ldcv(reinterpret_cast<const uint4*>(a.part[q] + (long)r * a.cols + c));
-        const half* h = reinterpret_cast<const half*>(&v);
+#pragma unroll
+      for (int q = 0; q < kMaxRanks; ++q) {
+        if (q >= a.world) break;
+        const half* h = reinterpret_cast<const half*>(&v[q]);
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[j] += __half2float(h[j]);
       }

@@ -131,6 +131,11 @@ struct AttnArgs {
   // the pages are not written by the kernel before this one on the stream
   // (true in the decode step): the K/V stream may start before its wait
   bool kv_static = false;
+  // prefill: blocks of the pool (tensor-map extent), the leading items that
+  // go to the tensor-core kernel, and the error word of bounded waits
+  int pool_blocks = 0;
+  int prefill_tc_items = 0;
+  unsigned* err = nullptr;
 };
 
 // fused = 1: apply RoPE to q and append the row's own k/v (one query row per
@@ -152,7 +157,14 @@ inline int decode_attn_splits(int num_sms, long rows, int Hkv) {
 // sequence (attention_prefill.cu). prefill_items cuts the batch's rows
 // (row_seq: sequence of each row, rows of a sequence consecutive) into
 // items (first row, rows); at most T items.
-int prefill_items(const int32_t* row_seq, int T, int2* items_host);
+// Items for head layout (D, rep): with the tensor-core kernel, up to
+// 128 / rep positions each, those too small for it (at most 16 positions and
+// fewer than 64 tile rows) last and cut to at most 16 positions; *n_tc = the
+// leading items for the tensor-core kernel. Without it, items of <= 16 rows.
+int prefill_items(const int32_t* row_seq, int T, int D, int rep, int2* items_host, int* n_tc);
+bool prefill_tc_supported(int D, int rep);
+// attention_prefill_tc.cu: the leading items on tcgen05 (see there)
+nmx_status_t paged_prefill_attention_tc(Ctx* c, const AttnArgs& a, const int2* items, int n_items);
 nmx_status_t paged_prefill_attention(Ctx* c, const AttnArgs& a, const int2* items, int n_items);
 // the tensor-core implementation behind paged_attention (attention_mma.cu)
 nmx_status_t paged_attention_mma(Ctx* c, const AttnArgs& a, bool fused);

@@ -621,6 +621,7 @@ nmx_status_t Model::run_layers_prefill(KvPool* pool, int T) {
     at.tok_seq = tok_seq; at.tok_pos = tok_pos; at.out = attn;
     at.T = T; at.Hq = cf.n_heads; at.Hkv = cf.n_kv_heads; at.D = cf.head_dim; at.BT = kBT;
     at.splits = 1; at.scale = 1.0f / std::sqrt(float(cf.head_dim));
+    at.pool_blocks = pool->num_blocks; at.prefill_tc_items = n_pf_tc; at.err = c->dev_err;
     NMX_TRY(paged_prefill_attention(c, at, pf_items, n_pf_items));
 
     NMX_TRY(block_out(ly.o, attn, Nq, T, 0));
@@ -756,9 +757,10 @@ nmx_status_t Model::upload_batch(const nmx_seq_t* seqs, int n, int* T_out, bool*
                                 size_t(n), cudaMemcpyHostToDevice, c->stream));
   h2d_bytes_last = size_t(T) * 12 + size_t(n) * 4 + size_t(n) * nb_max * 4;
   n_pf_items = 0;
+  n_pf_tc = 0;
   if (!decode) {
     int2* items = reinterpret_cast<int2*>(tbl + size_t(max_batch) * kBlockCap);
-    n_pf_items = prefill_items(sq, T, items);
+    n_pf_items = prefill_items(sq, T, cfg.head_dim, cfg.n_heads / cfg.n_kv_heads, items, &n_pf_tc);
     NMX_CUDA_OK(cudaMemcpyAsync(pf_items, items, size_t(n_pf_items) * 8, cudaMemcpyHostToDevice, c->stream));
     h2d_bytes_last += size_t(n_pf_items) * 8;
   }

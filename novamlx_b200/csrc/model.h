@@ -65,6 +65,7 @@ struct Model {
   int *tok_ids = nullptr, *tok_seq = nullptr, *tok_pos = nullptr, *last_rows = nullptr, *out_ids = nullptr;
   int2* pf_items = nullptr;  // prefill attention work items of the current batch
   int n_pf_items = 0;
+  int n_pf_tc = 0;  // leading items for the tensor-core prefill attention
   int *block_tables = nullptr, *hist = nullptr, *step = nullptr;
   float* inv_freq = nullptr;
   char* pinned = nullptr;

@@ -453,6 +453,129 @@ nmx_status_t launch_one(Ctx* c, const GemvArgs& a, int M) {
   return launch(c, kern, dim3(grid), dim3(kThreads), smem, b, num_tg);
 }
 
+// ---------------------------------------------------------------------------
+// Few-row fast path (M <= 8, 4-bit, f16, plain store): the operator-level
+// quantized matmul of a handful of rows (the engine's QuantizedLinear call on
+// a short prompt, MLX.quantizedMM in BailingHybridModel.swift:213).
+//
+// A CTA owns one 16-row tile; its eight warps take the tile's 128-k steps
+// round-robin, so there is no CTA-wide activation prologue: each lane loads
+// the 16 bytes of packed weights of rows g and g+8 it needs per step (words
+// 4t..4t+3, k = 32t .. 32t+31 of the step), its two rows' group scale and
+// bias, and 64 bytes of activation row g straight into registers, with the
+// next step's loads in flight while it computes. Weights are dequantised to
+// f16 (q exact, then w = q·s + b rounded once, as MLX's own large-row kernel
+// stages them) and fed to mma.sync m16n8k16; the MMA's k order is a
+// permutation of the step's 128 k that both operands share: lane t's pair
+// (q_i, q_{i+4}) of word j meets activations (x_{8j+i}, x_{8j+i+4}). The
+// eight warps' fp32 tiles are summed in warp order through shared memory.
+constexpr int kMlxWarps = 8;
+
+__device__ __forceinline__ uint32_t hsub2_u(uint32_t a, uint32_t b) {
+  __half2 r = __hsub2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t hfma2_u(uint32_t a, __half2 s, __half2 b) {
+  __half2 r = __hfma2(*reinterpret_cast<__half2*>(&a), s, b);
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+template <int GS>
+__global__ void __launch_bounds__(kMlxWarps * 32, 2) qgemv_mlx4_small_kernel(GemvArgs a) {
+  __shared__ float red[kMlxWarps][16][8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int K = a.K, M = a.M, wpr = K / 8, ng = K / GS, steps = K / 128;
+  const long r0 = long(blockIdx.x) * 16 + g;
+  const uint32_t* w0 = a.w + r0 * wpr + 4 * t;
+  const uint32_t* w1 = w0 + 8L * wpr;
+  const half* S = static_cast<const half*>(a.s);
+  const half* B = static_cast<const half*>(a.b);
+  const half* X = static_cast<const half*>(a.x) + long(g < M ? g : 0) * a.ldx + 32 * t;
+  const bool has_col = g < M;
+
+  struct Step {
+    uint4 wa, wb;      // rows g, g+8: 32 nibbles each
+    half sa, ba, sb, bb;
+    uint4 x[4];        // x[g][32t .. 32t+31] of the step
+  };
+  auto load = [&](Step& st, int k) {
+    st.wa = *reinterpret_cast<const uint4*>(w0 + k * 16);
+    st.wb = *reinterpret_cast<const uint4*>(w1 + k * 16);
+    const int G = (k * 128 + 32 * t) / GS;
+    st.sa = S[r0 * ng + G];
+    st.ba = B[r0 * ng + G];
+    st.sb = S[(r0 + 8) * ng + G];
+    st.bb = B[(r0 + 8) * ng + G];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      st.x[i] = has_col ? reinterpret_cast<const uint4*>(X + k * 128)[i] : make_uint4(0, 0, 0, 0);
+  };
+  float d[4] = {0.f, 0.f, 0.f, 0.f};
+  auto compute = [&](const Step& st) {
+    const uint32_t magic = 0x64006400u;  // f16 1024.0 in both halves
+    const __half2 sa2 = __halves2half2(st.sa, st.sa), ba2 = __halves2half2(st.ba, st.ba);
+    const __half2 sb2 = __halves2half2(st.sb, st.sb), bb2 = __halves2half2(st.bb, st.bb);
+    const uint32_t wa[4] = {st.wa.x, st.wa.y, st.wa.z, st.wa.w};
+    const uint32_t wb[4] = {st.wb.x, st.wb.y, st.wb.z, st.wb.w};
+    const uint32_t xs[16] = {st.x[0].x, st.x[0].y, st.x[0].z, st.x[0].w, st.x[1].x, st.x[1].y, st.x[1].z, st.x[1].w,
+                             st.x[2].x, st.x[2].y, st.x[2].z, st.x[2].w, st.x[3].x, st.x[3].y, st.x[3].z, st.x[3].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      // word j of each row: pairs (q_i, q_{i+4}), i = 0..3, as f16 weights
+      uint32_t A[4], Bw[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        A[i] = hfma2_u(hsub2_u(and_or(wa[j] >> (4 * i), 0x000F000Fu, magic), magic), sa2, ba2);
+        Bw[i] = hfma2_u(hsub2_u(and_or(wb[j] >> (4 * i), 0x000F000Fu, magic), magic), sb2, bb2);
+      }
+      // activations k = 8j .. 8j+7 of the lane's 32: pairs (x_i, x_{i+4})
+      const uint32_t X0 = xs[4 * j], X1 = xs[4 * j + 1], X2 = xs[4 * j + 2], X3 = xs[4 * j + 3];
+      const uint32_t p0 = __byte_perm(X0, X2, 0x5410), p1 = __byte_perm(X0, X2, 0x7632);
+      const uint32_t p2 = __byte_perm(X1, X3, 0x5410), p3 = __byte_perm(X1, X3, 0x7632);
+      // two k16 steps: (pairs 0, 1) and (pairs 2, 3)
+      mma16816(d, A[0], Bw[0], A[1], Bw[1], p0, p1, d[0], d[1], d[2], d[3]);
+      mma16816(d, A[2], Bw[2], A[3], Bw[3], p2, p3, d[0], d[1], d[2], d[3]);
+    }
+  };
+  grid_wait();
+  Step cur, nxt;
+  int k = warp;
+  if (k < steps) load(cur, k);
+  for (; k < steps; k += kMlxWarps) {
+    if (k + kMlxWarps < steps) load(nxt, k + kMlxWarps);
+    compute(cur);
+    cur = nxt;
+  }
+  grid_launch_dependents();
+  red[warp][g][2 * t] = d[0];
+  red[warp][g][2 * t + 1] = d[1];
+  red[warp][g + 8][2 * t] = d[2];
+  red[warp][g + 8][2 * t + 1] = d[3];
+  __syncthreads();
+  for (int e = threadIdx.x; e < 16 * M; e += kMlxWarps * 32) {
+    const int r = e % 16, m = e / 16;
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMlxWarps; ++w) v += red[w][r][m];
+    static_cast<half*>(a.y)[long(m) * a.ldy + long(blockIdx.x) * 16 + r] = __float2half_rn(v);
+  }
+}
+
+bool mlx4_small_ok(const GemvArgs& a, int bits, int gs, nmx_dtype_t dt, int epi) {
+  return bits == 4 && (gs == 32 || gs == 64 || gs == 128) && dt == NMX_F16 && epi == EPI_STORE &&
+         a.M >= 1 && a.M <= 8 && a.gamma == nullptr && a.bias == nullptr && a.K % 128 == 0 && a.N % 16 == 0 &&
+         reinterpret_cast<uintptr_t>(a.x) % 16 == 0 && (a.ldx * 2) % 16 == 0 &&
+         reinterpret_cast<uintptr_t>(a.w) % 16 == 0;
+}
+
+nmx_status_t launch_mlx4_small(Ctx* c, const GemvArgs& a, int gs) {
+  const dim3 grid(a.N / 16), block(kMlxWarps * 32);
+  if (gs == 64) return launch(c, qgemv_mlx4_small_kernel<64>, grid, block, 0, a);
+  if (gs == 32) return launch(c, qgemv_mlx4_small_kernel<32>, grid, block, 0, a);
+  return launch(c, qgemv_mlx4_small_kernel<128>, grid, block, 0, a);
+}
+
 template <typename T, int BITS, int GS>
 nmx_status_t dispatch_nt(Ctx* c, const GemvArgs& a, int M, int epi) {
   if (M <= 8) {
@@ -509,6 +632,7 @@ nmx_status_t qgemv(Ctx* c, const GemvArgs& a, int bits, int gs, nmx_dtype_t dt, 
   NMX_CHECK(mmax > 0, NMX_ERR_UNSUPPORTED, "qgemv: K too large for shared-memory staging");
   NMX_CHECK(epi != EPI_ARGMAX || a.M <= std::min(mmax, 32), NMX_ERR_UNSUPPORTED,
             "qgemv: argmax epilogue needs all rows in one launch");
+  if (mlx4_small_ok(a, bits, gs, dt, epi)) return launch_mlx4_small(c, a, gs);
   const size_t esz = 2;
   for (int m0 = 0; m0 < a.M; m0 += mmax) {
     const int mc = std::min(mmax, a.M - m0);

@@ -21,7 +21,9 @@ def tiny_cfgs():
     qwen = dict(vocab=1024, hidden=512, n_layers=2, n_heads=4, n_kv_heads=2, head_dim=128, ffn=1536,
                 qkv_bias=True, rope_theta=1e6, rms_eps=1e-6)
     l8 = dict(llama, bits=8, group_size=32)
-    return {"llama": llama, "qwen": qwen, "llama8": l8}
+    # one q head per kv head: 128-position items in the prefill attention
+    mha = dict(llama, n_kv_heads=8)
+    return {"llama": llama, "qwen": qwen, "llama8": l8, "mha": mha}
 
 
 @pytest.fixture(scope="module")
@@ -233,10 +235,12 @@ def test_wide_layer_matches_oracle(ctx):
         pos += 1
 
 
-@pytest.mark.parametrize("name", ["llama", "qwen"])
+@pytest.mark.parametrize("name", ["llama", "qwen", "mha"])
 def test_prefill_tensor_core_path_matches_oracle(ctx, name):
     """A prompt long enough for the tcgen05 GEMM path (>= 64 rows, ragged
-    last tile), then decode steps over the pages it wrote."""
+    last tile) and the tcgen05 prefill attention (128-row tiles of
+    positions x q heads, a ragged last item on the small-item kernel), then
+    decode steps over the pages it wrote."""
     from novamlx_b200 import nmx
     m, om, cfg = build(ctx, name)
     pool = nmx.KVPool(m, 64)
