@@ -70,7 +70,7 @@ constexpr int kRSMax = 16;                  // raw record slots
 using tc::kRecPad;                          // shared-memory stride of a record
 constexpr int kRawSlot = 8 * kRecPad;       // the 8 records of one tile and K block
 constexpr int kMaxTG = 16;                  // weight tiles per CTA
-constexpr int kMaxNT = 128;
+constexpr int kMaxNT = kTcsMaxRows;
 constexpr size_t kSmemCap = 225 * 1024;  // dynamic shared memory the kernel may ask for (plus 1 KB static)
 
 struct TcsArgs {
@@ -604,14 +604,20 @@ TcsPlan plan_tcs(int M, int N_out, int K, int epi, int num_sms) {
       }
     }
   }
-  // x stages to cover the L2 latency of the x tiles (shared by tg units),
-  // the rest of shared memory for raw record slots
+  // The four dequantising warpgroups take units round-robin from the raw
+  // ring, so the ring holds a multiple of kDG slots: the unit a warpgroup
+  // waits for then reuses a slot whose previous unit it consumed itself, and
+  // a phase-parity wait can never run two phases ahead. Eight slots where
+  // they fit (four at the widest x tiles), x stages to cover the L2 latency
+  // of the x tiles (shared by tg units), then more raw slots.
   const size_t xstage = size_t(2) * p.NT * 128;
   const size_t a_bytes = size_t(kAST) * kAStageBytes;
-  p.xs = std::max(2, std::min(kXSMax, int((kSmemCap - 1024 - a_bytes - 3 * size_t(kRawSlot)) / xstage)));
+  const size_t avail = kSmemCap - 1024 - a_bytes;
+  const int rs_min = avail >= 2 * xstage + 2 * kDG * size_t(kRawSlot) ? 2 * kDG : kDG;
+  p.xs = std::max(2, std::min(kXSMax, int((avail - rs_min * size_t(kRawSlot)) / xstage)));
   p.xs = std::min(p.xs, std::max(2, 8 / std::max(1, p.tg / (epi == EPI_SILU ? 2 : 1))));
   const size_t fixed = size_t(p.xs) * xstage + a_bytes + 1024;
-  p.rs = int(std::min<size_t>(kRSMax, (kSmemCap - fixed) / kRawSlot));
+  p.rs = int(std::min<size_t>(kRSMax, (kSmemCap - fixed) / kRawSlot)) / kDG * kDG;
   p.smem = fixed + size_t(p.rs) * kRawSlot;
   p.partial_floats = p.S > 1 ? size_t(p.groups) * p.S * p.tg * p.NT * 128 : 0;
   return p;
@@ -657,6 +663,8 @@ nmx_status_t qgemm_tcs(Ctx* c, const GemvDLArgs& a, int epi) {
             "qgemm_tcs: x must be 16-byte aligned with a 16-byte row pitch");
   NMX_CHECK(reinterpret_cast<uintptr_t>(a.w) % 16 == 0, NMX_ERR_INVALID, "qgemm_tcs: records must be 16-byte aligned");
   const TcsPlan p = plan_tcs(a.M, a.N, a.K, epi, c->num_sms);
+  NMX_CHECK(p.rs >= kDG && p.rs % kDG == 0 && p.smem <= kSmemCap, NMX_ERR_UNSUPPORTED,
+            "qgemm_tcs: shared-memory plan does not fit");
   if (p.S > 1) {
     NMX_CHECK(a.partials != nullptr && a.partials_cap >= p.partial_floats && a.counters != nullptr,
               NMX_ERR_INVALID, "qgemm_tcs: partial-sum scratch too small");

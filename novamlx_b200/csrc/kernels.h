@@ -96,7 +96,7 @@ constexpr int kGemmMinRows = 64;  // qgemv_dl hands row counts from here on to q
 // activation rows as its N, K split over the SMs): 1..128 rows, N_out % 128,
 // K % 128; store / residual / SiLU·up epilogues, no RMSNorm prologue
 constexpr int kTcsMinRows = 9;    // qgemv_dl hands kTcsMinRows..kTcsMaxRows rows to qgemm_tcs
-constexpr int kTcsMaxRows = 128;
+constexpr int kTcsMaxRows = 112;  // the decode GEMM's shared-memory budget: x tiles of <= 112 rows
 bool qgemm_tcs_supported(int M, int N_out, int K, int epi);
 // floats of partial-sum scratch (partials) and counters one launch needs
 size_t qgemm_tcs_partials_floats(int M, int N_out, int K, int epi, int num_sms);
