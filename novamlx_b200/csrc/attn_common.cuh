@@ -62,5 +62,112 @@ __device__ __forceinline__ void rope2(float a, float b, float ang, float& ra, fl
   rb = b * cs + a * sn;
 }
 
+// ---------------------------------------------------------------------------
+// Quantized KV pages (the kvBits path). A page record holds one (block, kv
+// head) of K or V for 16 tokens: codes [16][D * bits / 32] u32 (MLX packing,
+// low bits first along d), then scales [16][D / gs] and biases [16][D / gs]
+// f16 — MLX-affine quantization in groups of gs along head_dim.
+__host__ __device__ constexpr int kv_page_bytes(int D, int bits, int gs) {
+  return bits == 0 ? 16 * D * 2 : 16 * (D * bits / 8 + 2 * (D / gs) * 2);
+}
+
+// One K or V row held by a warp (lane l: values d = l * VPL .. + VPL - 1),
+// quantized in groups of gs: scale = (max - min) / (2^bits - 1) and bias =
+// min in fp32 for the codes, stored as f16; the row's codes, scales and
+// biases go to slot `tok` of the page record `rec`, and v returns the
+// dequantized values (q * s + b with the f16 scale and bias, one rounding).
+template <int D>
+__device__ __forceinline__ void quantize_row_warp(float* v, int bits, int gs, unsigned char* rec, int tok) {
+  constexpr int VPL = D / 32;
+  const int lane = threadIdx.x & 31;
+  const int lpg = gs / VPL;  // lanes per group: a power of two <= 32
+  float mn = v[0], mx = v[0];
+#pragma unroll
+  for (int i = 1; i < VPL; ++i) {
+    mn = fminf(mn, v[i]);
+    mx = fmaxf(mx, v[i]);
+  }
+  for (int o = lpg / 2; o > 0; o >>= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  const float nbins = float((1 << bits) - 1);
+  const float scale = (mx - mn) / nbins, bias = mn;
+  const half s16 = __float2half_rn(scale), b16 = __float2half_rn(bias);
+  uint32_t packed = 0;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    float q = 0.f;
+    if (scale > 0.f) q = fminf(fmaxf(rintf((v[i] - bias) / scale), 0.f), nbins);
+    packed |= uint32_t(q) << (i * bits);
+    v[i] = __half2float(__hfma(__float2half_rn(q), s16, b16));
+  }
+  // a 32-bit word holds the codes of lpw consecutive lanes
+  const int lpw = 32 / (bits * VPL);
+  uint32_t word = packed;
+  for (int o = 1; o < lpw; o <<= 1) {
+    const uint32_t other = __shfl_down_sync(0xffffffffu, word, o);
+    if ((lane & (2 * o - 1)) == 0) word |= other << (o * bits * VPL);
+  }
+  const int rowbytes = D * bits / 8, ng = D / gs;
+  if ((lane % lpw) == 0) reinterpret_cast<uint32_t*>(rec + tok * rowbytes)[lane / lpw] = word;
+  if ((lane % lpg) == 0) {
+    half* sc = reinterpret_cast<half*>(rec + 16 * rowbytes);
+    sc[tok * ng + lane / lpg] = s16;
+    sc[16 * ng + tok * ng + lane / lpg] = b16;
+  }
+}
+
+// 8 f16 values w = s * q + b (k order) from one 32-bit word of 4-bit codes
+__device__ __forceinline__ uint4 dq4_chunk(uint32_t w, __half2 s2, __half2 b2) {
+  const uint32_t magic = 0x64006400u;  // f16 1024.0 in both halves
+  const __half2 k1024 = __float2half2_rn(1024.f);
+  uint32_t p[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t t;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(t) : "r"(w >> (4 * i)), "r"(0x000F000Fu), "r"(magic));
+    __half2 h = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&t), k1024), s2, b2);  // (w_i, w_{i+4})
+    p[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return make_uint4(__byte_perm(p[0], p[1], 0x5410), __byte_perm(p[2], p[3], 0x5410),
+                    __byte_perm(p[0], p[1], 0x7632), __byte_perm(p[2], p[3], 0x7632));
+}
+// 8 f16 values from two 32-bit words of 8-bit codes
+__device__ __forceinline__ uint4 dq8_chunk(uint2 w, __half2 s2, __half2 b2) {
+  const __half2 k1024 = __float2half2_rn(1024.f);
+  uint32_t r[4];
+  const uint32_t src[2] = {w.x, w.y};
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      uint32_t t = __byte_perm(src[j], 0x64646464u, e ? 0x7362 : 0x5140);  // 1024 + byte, two of them
+      __half2 h = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&t), k1024), s2, b2);
+      r[2 * j + e] = *reinterpret_cast<uint32_t*>(&h);
+    }
+  }
+  return make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+// One page record dequantized by a warp into a swizzled [16][D] f16 tile.
+template <int D>
+__device__ __forceinline__ void dequant_page_warp(const unsigned char* rec, int bits, int gs, unsigned char* tile) {
+  constexpr int CH = D / 8;
+  const int lane = threadIdx.x & 31;
+  const int rowbytes = D * bits / 8, ng = D / gs;
+  const half* sc = reinterpret_cast<const half*>(rec + 16 * rowbytes);
+  const half* bi = sc + 16 * ng;
+#pragma unroll 4
+  for (int i = lane; i < 16 * CH; i += 32) {
+    const int r = i / CH, c = i % CH;
+    const int g = (8 * c) / gs;
+    const __half2 s2 = __half2half2(sc[r * ng + g]), b2 = __half2half2(bi[r * ng + g]);
+    const uint4 o = bits == 4 ? dq4_chunk(*reinterpret_cast<const uint32_t*>(rec + r * rowbytes + 4 * c), s2, b2)
+                              : dq8_chunk(*reinterpret_cast<const uint2*>(rec + r * rowbytes + 8 * c), s2, b2);
+    *reinterpret_cast<uint4*>(tile + swz<D>(r, c)) = o;
+  }
+}
+
 }  // namespace
 }  // namespace nmx

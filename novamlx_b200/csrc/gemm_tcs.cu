@@ -17,16 +17,13 @@
 //     boxes of 64 k × NT rows, SWIZZLE_128B, rows past M read as zeros);
 //   * four warpgroups (warps 0-15) take the (block, tile) units in turn:
 //     each thread reads one weight row of the unit (64 bytes, conflict-free:
-//     see lane_row) and writes its 128 f16 weights w = s·q + b as row L of
-//     one of four shared-memory A stages (K-major, 128-byte swizzle). The
-//     stages live in shared memory, not TMEM: with the A operand in TMEM the
-//     dequantising warps' tcgen05.st traffic and the MMAs' A reads contended
-//     for TMEM and doubled the MMAs' time at these widths;
-//   * one thread of warp 16 issues eight tcgen05.mma (A and x from shared
-//     memory; M = 128, N = NT, K = 16) per unit into that tile's
-//     accumulator (TMEM columns tile·NT ...; all 512 columns hold
-//     accumulators), committing the A stage (and after the group's last
-//     tile the x tile) back to its producers.
+//     see lane_row) and writes its 128 f16 weights w = s·q + b straight into
+//     its TMEM lane with tcgen05.st, into one of four 64-column A stages, so
+//     the dequantized tile never touches shared memory;
+//   * one thread of warp 16 issues eight tcgen05.mma (A from TMEM, x from
+//     shared memory; M = 128, N = NT, K = 16) per unit into that tile's
+//     accumulator (TMEM columns tile·NT ...), committing the A stage (and
+//     after the group's last tile the x tile) back to its producers.
 // After the last block warps 0-15 read the accumulators (tcgen05.ld 32x32b;
 // warp w: lanes 32 (w % 4) .., every fourth 8-column chunk). With one K share they run
 // the epilogue directly; with S shares each CTA stores its f32 partial
@@ -62,9 +59,9 @@ constexpr int kDG = 4;                      // dequant warpgroups (they take uni
 constexpr int kSDW = 4 * kDG;               // dequant / epilogue warps
 constexpr int kSThreads = (kSDW + 3) * 32;  // + MMA, x-tile and record-loader warps
 constexpr int kSWMma = kSDW, kSWTma = kSDW + 1, kSWRec = kSDW + 2;
-constexpr int kAST = 4;                     // dequantized weight stages, in shared memory
-constexpr int kAStageBytes = 128 * 128 * 2; // 128 rows x 128 k of f16: two 64-k swizzled halves
-constexpr int kAccCols = 512;               // TMEM holds only the accumulators
+constexpr int kAST = 4;                     // dequantized weight stages, in TMEM
+constexpr int kAStageCols = 64;             // 128 k of f16, two per 32-bit column
+constexpr int kAccCols = 512 - kAST * kAStageCols;  // accumulator columns
 constexpr int kXSMax = 8;                   // x stages
 constexpr int kRSMax = 16;                  // raw record slots
 using tc::kRecPad;                          // shared-memory stride of a record
@@ -175,8 +172,30 @@ __device__ __forceinline__ void lane_row(int L, int& r8, int& g16) {
   g16 = 8 * ((Q >> 1) & 1) + 2 * (Q >> 2) + (j >> 2);
 }
 
+// D[tmem] (+)= A[tmem] · B[smem]ᵀ, kind::f16
+__device__ __forceinline__ void mma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p; }" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 consecutive 32-bit columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
 // the 16 words of one record row (both groups) as 128 f16 weights
-// w = s·q + b, two per 32-bit word in k order: group gi in out[gi]
+// w = s·q + b, two per 32-bit column in k order: group gi in out[gi]
 __device__ __forceinline__ void dequant_row_words(const uint4* c, __half2 s2[2], __half2 s16[2], __half2 b2[2],
                                                   uint32_t out[2][32]) {
   const __half2 k1024 = __float2half2_rn(1024.f);
@@ -237,8 +256,7 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
   const int NT = a.NT;
   const int xhalf = NT * 128;    // bytes of one 64-k half of an x stage
   unsigned char* stX = smem;
-  unsigned char* stA = stX + a.xs * 2 * xhalf;  // 1024-aligned: xhalf is a multiple of 2 KB
-  unsigned char* raw = stA + kAST * kAStageBytes;
+  unsigned char* raw = stX + a.xs * 2 * xhalf;
 
   if (tid == 0) {
     for (int s = 0; s < kAST; ++s) {
@@ -325,9 +343,7 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
       // (descriptor start addresses advance in 16-byte units)
       const uint64_t xdesc0 = smem_desc(stX);
       const uint32_t xstage_d = uint32_t(2 * xhalf) >> 4, xhalf_d = uint32_t(xhalf) >> 4;
-      const uint64_t adesc0 = smem_desc(stA);
-      const uint32_t astage_d = uint32_t(kAStageBytes) >> 4, ahalf_d = uint32_t(kAStageBytes / 2) >> 4;
-      const uint32_t idesc = a.idesc;
+      const uint32_t a0 = taddr + uint32_t(kAccCols), idesc = a.idesc;
       int ti = 0, as = 0, aph = 0, xs = 0, xph = 0;
       uint32_t first = 0u;  // 0 until the first block is in the accumulators
       for (int i = 0; i < units; ++i) {
@@ -341,11 +357,11 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
         tc::tc_fence_after();
         const uint64_t bd = xdesc0 + uint64_t(xs * xstage_d);
         const uint32_t d = taddr + uint32_t(ti * NT);
-        const uint64_t ad = adesc0 + uint64_t(as * astage_d);
+        const uint32_t A = a0 + uint32_t(as * kAStageCols);
 #pragma unroll
         for (int k16 = 0; k16 < 8; ++k16)
-          tc::mma_f16(d, ad + uint64_t((k16 >> 2) * ahalf_d + 2 * (k16 & 3)),
-                      bd + uint64_t((k16 >> 2) * xhalf_d + 2 * (k16 & 3)), idesc, k16 ? 1u : first);
+          mma_f16_ta(d, A + 8 * k16, bd + uint64_t((k16 >> 2) * xhalf_d + 2 * (k16 & 3)), idesc,
+                     k16 ? 1u : first);
         tc::mma_commit(&a_empty[as]);
         if (++as == kAST) {
           as = 0;
@@ -372,6 +388,7 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
     lane_row(L, r8, g16);
     const int rowoff = r8 * kRecPad + (g16 >> 3) * 512 + 64 * (g16 & 7);
     const int sboff = r8 * kRecPad + 1024 + (g16 & 7) * 4 + (g16 >> 3) * 2;
+    const uint32_t lane_base = taddr + (uint32_t(32 * (warp & 3)) << 16);
     static_assert(kDG == kAST, "warpgroup dg owns A stage dg");
     const int as = dg;
     int rs = dg % a.rs, rph = (dg / a.rs) & 1;
@@ -402,15 +419,12 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
       uint32_t out[2][32];
       dequant_row_words(c, s2, s16, b2, out);
       mbar_arrive(&raw_empty[rs]);  // the slot's bytes are in registers
-      // row L of the stage's K-major tile, two 64-k halves in the 128-byte swizzle
-      unsigned char* arow = stA + as * kAStageBytes;
-#pragma unroll
-      for (int gi = 0; gi < 2; ++gi)
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch)
-          *reinterpret_cast<uint4*>(arow + gi * (kAStageBytes / 2) + tc::sw128(L, ch)) =
-              make_uint4(out[gi][4 * ch], out[gi][4 * ch + 1], out[gi][4 * ch + 2], out[gi][4 * ch + 3]);
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor core
+      tc::tc_fence_after();         // after the wait for the stage's last MMAs
+      const uint32_t acol = lane_base + uint32_t(kAccCols + as * kAStageCols);
+      tmem_st32(acol, out[0]);
+      tmem_st32(acol + 32, out[1]);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc::tc_fence_before();
       mbar_arrive(&a_full[as]);
       rs += kDG;
       while (rs >= a.rs) {
@@ -604,19 +618,18 @@ TcsPlan plan_tcs(int M, int N_out, int K, int epi, int num_sms) {
       }
     }
   }
-  // The four dequantising warpgroups take units round-robin from the raw
-  // ring, so the ring holds a multiple of kDG slots: the unit a warpgroup
-  // waits for then reuses a slot whose previous unit it consumed itself, and
-  // a phase-parity wait can never run two phases ahead. Eight slots where
-  // they fit (four at the widest x tiles), x stages to cover the L2 latency
-  // of the x tiles (shared by tg units), then more raw slots.
+  // Shared memory: eight raw record slots first, then as many x stages as
+  // fit (up to kXSMax), then more raw slots. An x tile comes from L2 and a
+  // block of tg units can take less time than that round trip, so the x
+  // ring, not the records, sets the pace when it is shallow (two stages at
+  // three tiles per group measured half the MMA-issue rate). The four
+  // dequantising warpgroups take units round-robin from the raw ring, so it
+  // holds a multiple of kDG slots: the unit a warpgroup waits for then reuses
+  // a slot whose previous unit it consumed itself, and a phase-parity wait
+  // can never run two phases ahead.
   const size_t xstage = size_t(2) * p.NT * 128;
-  const size_t a_bytes = size_t(kAST) * kAStageBytes;
-  const size_t avail = kSmemCap - 1024 - a_bytes;
-  const int rs_min = avail >= 2 * xstage + 2 * kDG * size_t(kRawSlot) ? 2 * kDG : kDG;
-  p.xs = std::max(2, std::min(kXSMax, int((avail - rs_min * size_t(kRawSlot)) / xstage)));
-  p.xs = std::min(p.xs, std::max(2, 8 / std::max(1, p.tg / (epi == EPI_SILU ? 2 : 1))));
-  const size_t fixed = size_t(p.xs) * xstage + a_bytes + 1024;
+  p.xs = std::max(2, std::min(kXSMax, int((kSmemCap - 1024 - 2 * kDG * size_t(kRawSlot)) / xstage)));
+  const size_t fixed = size_t(p.xs) * xstage + 1024;
   p.rs = int(std::min<size_t>(kRSMax, (kSmemCap - fixed) / kRawSlot)) / kDG * kDG;
   p.smem = fixed + size_t(p.rs) * kRawSlot;
   p.partial_floats = p.S > 1 ? size_t(p.groups) * p.S * p.tg * p.NT * 128 : 0;

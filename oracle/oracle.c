@@ -29,6 +29,13 @@
  *     (after every linear, bias add, RoPE, attention, residual add, norm,
  *     silu and gating multiply). RoPE frequencies follow Llama-3.1's
  *     "llama3" scaling when rope_factor > 0.
+ *   - Quantized KV cache (the kvBits path: TurboQuantService.
+ *     applyToGenerateParameters, Sources/NovaMLXEngine/TurboQuantCache.swift:
+ *     78-104, which turns on mlx-swift-lm's quantized KV cache): with
+ *     kv_bits > 0 every appended K row (after RoPE) and V row is quantized by
+ *     the rule above in groups of kv_gs along head_dim and stored
+ *     dequantized (w = q * s + b with the f16 scale and bias); attention
+ *     then reads those values.
  *   - Greedy sampling: argmax, lowest index on ties
  *     (Sources/NovaMLXEngine/CompiledSampler.swift:24-27) and the frequency
  *     penalty (Sources/NovaMLXEngine/FusedBatchScheduler.swift:1218-1227).
@@ -501,7 +508,34 @@ typedef struct {
   const uint16_t *q_s, *k_s, *v_s, *o_s, *g_s, *u_s, *d_s;
   const uint16_t *q_b, *k_b, *v_b, *o_b, *g_b, *u_b, *d_b;
   const uint16_t *q_bias, *k_bias, *v_bias; /* [L, n] or NULL */
+  int kv_bits, kv_gs;                        /* quantized KV cache (0: f16 cache) */
 } oracle_model_t;
+
+/* One cached K or V row quantized and dequantized in place: groups of gs
+ * along the row, scale = (max-min)/(2^bits-1) and bias = min in fp32 for
+ * the codes, the row rebuilt from the codes with the f16 scale and bias. */
+static void qdq_row(uint16_t* row, int D, int bits, int gs, int dt) {
+  const int nbins = (1 << bits) - 1;
+  for (int g = 0; g < D / gs; ++g) {
+    uint16_t* r = row + (size_t)g * gs;
+    float mn = ldv(r, 0, dt), mx = mn;
+    for (int i = 1; i < gs; ++i) {
+      const float v = ldv(r, i, dt);
+      mn = v < mn ? v : mn;
+      mx = v > mx ? v : mx;
+    }
+    const float scale = (mx - mn) / (float)nbins, bias = mn;
+    const float s16 = rnd(scale, dt), b16 = rnd(bias, dt);
+    for (int i = 0; i < gs; ++i) {
+      float q = 0.0f;
+      if (scale > 0.0f) {
+        q = rintf((ldv(r, i, dt) - bias) / scale);
+        q = q < 0.0f ? 0.0f : (q > (float)nbins ? (float)nbins : q);
+      }
+      r[i] = stv(fmaf(q, s16, b16), dt);
+    }
+  }
+}
 
 static void linear(const oracle_model_t* m, const float* x, int T, const uint32_t* w, const uint16_t* s,
                    const uint16_t* b, int N, int K, const uint16_t* bias, float* y) {
@@ -570,11 +604,18 @@ EXPORT int oracle_forward(const oracle_model_t* m, uint16_t* kcache, uint16_t* v
     uint16_t* KC = kcache + (size_t)l * Hkv * max_ctx * D;
     uint16_t* VC = vcache + (size_t)l * Hkv * max_ctx * D;
     for (int t = 0; t < T; ++t)
-      for (int hk = 0; hk < Hkv; ++hk)
+      for (int hk = 0; hk < Hkv; ++hk) {
+        uint16_t* kr = KC + ((size_t)hk * max_ctx + pos[t]) * D;
+        uint16_t* vr = VC + ((size_t)hk * max_ctx + pos[t]) * D;
         for (int d = 0; d < D; ++d) {
-          KC[((size_t)hk * max_ctx + pos[t]) * D + d] = k16[((size_t)t * Hkv + hk) * D + d];
-          VC[((size_t)hk * max_ctx + pos[t]) * D + d] = stv(vv[((size_t)t * Hkv + hk) * D + d], dt);
+          kr[d] = k16[((size_t)t * Hkv + hk) * D + d];
+          vr[d] = stv(vv[((size_t)t * Hkv + hk) * D + d], dt);
         }
+        if (m->kv_bits > 0) {
+          qdq_row(kr, D, m->kv_bits, m->kv_gs, dt);
+          qdq_row(vr, D, m->kv_bits, m->kv_gs, dt);
+        }
+      }
     attn_cache(q16, KC, VC, max_ctx, T, Hq, Hkv, D, start_pos, 1.0f / sqrtf((float)D), dt, o16);
     for (size_t i = 0; i < (size_t)T * Nq; ++i) att[i] = ldv(o16, i, dt);
     linear(m, att, T, m->o_w + (size_t)l * H * wpr_q, m->o_s + (size_t)l * H * ng_q,

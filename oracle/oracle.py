@@ -194,7 +194,7 @@ class _CModel(C.Structure):
                    "q_w", "k_w", "v_w", "o_w", "g_w", "u_w", "d_w",
                    "q_s", "k_s", "v_s", "o_s", "g_s", "u_s", "d_s",
                    "q_b", "k_b", "v_b", "o_b", "g_b", "u_b", "d_b",
-                   "q_bias", "k_bias", "v_bias")]
+                   "q_bias", "k_bias", "v_bias")] + [("kv_bits", C.c_int), ("kv_gs", C.c_int)]
 
 
 _LIN = {"q": "self_attn.q_proj", "k": "self_attn.k_proj", "v": "self_attn.v_proj", "o": "self_attn.o_proj",
@@ -220,6 +220,8 @@ class TinyCfg:
     rope_low_freq_factor: float = 1.0
     rope_high_freq_factor: float = 4.0
     rope_original_max_pos: int = 8192
+    kv_bits: int = 0      # quantized KV cache: 4 or 8 (0: f16 cache)
+    kv_group_size: int = 64
 
 
 class OracleModel:
@@ -240,6 +242,8 @@ class OracleModel:
         m.qkv_bias = int(bool(c.qkv_bias))
         m.tie = 0
         m.eps = float(c.rms_eps)
+        m.kv_bits = int(getattr(c, "kv_bits", 0))
+        m.kv_gs = int(getattr(c, "kv_group_size", 64))
 
         def keep(name, arr):
             arr = _c(arr)
