@@ -539,6 +539,26 @@ def run_c4(args, rank, world, dist, torch, nmx, ctx, peaks, dev, clk_box):
                       "frac_of_measured_bf16": round(flop / (pms * 1e-3) / 1e12 / (peaks["bf16_tflops"] * world), 4),
                       "note": "whole prompt in one nmx_forward, host call included"}
 
+    # the same decode over 4-bit KV pages (groups of 64 along head_dim): the
+    # quantized-KV path, pages filled with seeded random records
+    pool.close()
+    qpool = nmx.KVPool(m, C4_BATCH * nblk + 2, kv_bits=4, kv_group_size=64)
+    qpool.fill_random(seed=11 + rank, std=1.0)
+    m.decode_greedy(qpool, first, start, tables, 2, want_ids=False)
+    _barrier(dist)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(args.steps):
+        m.decode_greedy(qpool, first, start, tables, C4_GEN, want_ids=False)
+    e1.record()
+    torch.cuda.synchronize()
+    qms = _max_over_ranks(torch, dist, e0.elapsed_time(e1))
+    out["kv4"] = {"value": round(args.steps * C4_GEN * C4_BATCH / (qms / 1000.0), 2), "unit": "tok/s",
+                  "ms_per_step": round(qms / args.steps, 3), "kv_bits": 4, "kv_group_size": 64,
+                  "kv_bytes_per_token_per_rank": qpool.bytes_per_token,
+                  "note": "same decode, K/V pages quantized on append and dequantized in the attention kernel"}
+    qpool.close()
+
     # the exchange per call vs an NCCL all-reduce of the same 32 x 5120 f16
     if world > 1:
         part = torch.randn((C4_BATCH, cfg.hidden), device="cuda", dtype=torch.float16)
@@ -581,7 +601,6 @@ def run_c4(args, rank, world, dist, torch, nmx, ctx, peaks, dev, clk_box):
     out["weight_bytes_per_rank"] = m.step_weight_bytes
     out["kv_bytes_per_token_per_rank"] = m.kv_bytes_per_token
     m.close()
-    pool.close()
     return out
 
 
@@ -686,6 +705,7 @@ def _run_ours(args, rank, world, dist, torch, nmx, ctx, peaks, dev):
         "step_roofline": {"bytes_per_rank_per_decode_step": per_rank_bytes, "achieved": round(gbs, 1),
                           "peak": peaks["hbm_gbs"], "unit": "GB/s (per GPU)", "frac": round(gbs / peaks["hbm_gbs"], 4)},
         "prefill_8192": c4["prefill"],
+        "kv4_decode": c4["kv4"],
         "cpu_baseline": cpu,
         "e2e": c4["e2e"],
         "gpu_launches": c4["launches"],

@@ -292,6 +292,24 @@ NMX_API uint64_t nmx_model_step_weight_bytes(nmx_model_t model);
  * (Sources/NovaMLXPrefixCache/PagedBlockPool.swift:108-139). */
 NMX_API nmx_status_t nmx_kv_pool_create(nmx_model_t model, int block_tokens, int num_blocks,
                                         nmx_kv_pool_t* out);
+/* A paged KV pool whose pages hold MLX-affine quantized K and V: kv_bits 4
+ * or 8, groups of kv_group_size (32 or 64) along head_dim (64 or 128). Page
+ * record of one (block, kv head) of K or of V: codes [block_tokens]
+ * [head_dim * kv_bits / 32] u32 (low bits first), then scales and biases
+ * [block_tokens][head_dim / kv_group_size] f16. Appended rows are quantized
+ * on write (scale = (max - min) / (2^bits - 1), bias = min); attention reads
+ * the dequantized values. The kvBits path of the reference:
+ * TurboQuantService.applyToGenerateParameters
+ * (Sources/NovaMLXEngine/TurboQuantCache.swift:78-104) turns on
+ * mlx-swift-lm's quantized KV cache. Prefill attention over such pages runs
+ * on the small-item kernel; nmx_kv_read_blocks / nmx_kv_write_blocks move
+ * the raw page records (host layout [n][layers][2][Hkv * record bytes]). */
+NMX_API nmx_status_t nmx_kv_pool_create_quantized(nmx_model_t model, int block_tokens, int num_blocks,
+                                                  int kv_bits, int kv_group_size, nmx_kv_pool_t* out);
+/* KV bytes one token occupies in this pool over all layers (f16 or
+ * quantized pages): the budget figure of effectiveBytesPerToken
+ * (Sources/NovaMLXEngine/MLXEngine.swift:1368-1386). */
+NMX_API uint64_t nmx_kv_pool_bytes_per_token(nmx_kv_pool_t pool);
 NMX_API nmx_status_t nmx_kv_pool_destroy(nmx_kv_pool_t pool);
 /* Copy whole blocks src[i] → dst[i] in every layer (copy-on-write of a shared
  * partial block, and the device side of forkBlockTable,

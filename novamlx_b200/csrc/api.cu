@@ -433,6 +433,25 @@ NMX_API nmx_status_t nmx_kv_pool_create(nmx_model_t model, int block_tokens, int
   return NMX_OK;
 }
 
+NMX_API nmx_status_t nmx_kv_pool_create_quantized(nmx_model_t model, int block_tokens, int num_blocks, int kv_bits,
+                                                  int kv_group_size, nmx_kv_pool_t* out) {
+  API_BEGIN;
+  REQUIRE(model, "model");
+  REQUIRE(out, "output handle");
+  NMX_CHECK(kv_bits == 4 || kv_bits == 8, NMX_ERR_UNSUPPORTED, "quantized kv pool: bits must be 4 or 8");
+  KvPool* p = nullptr;
+  NMX_TRY(KvPool::create(model->m, block_tokens, num_blocks, &p, kv_bits, kv_group_size));
+  model->refs++;
+  *out = new nmx_kv_pool_s{p, model};
+  return NMX_OK;
+}
+
+NMX_API uint64_t nmx_kv_pool_bytes_per_token(nmx_kv_pool_t pool) {
+  if (!pool) return 0;
+  const KvPool* p = pool->p;
+  return uint64_t(p->block_bytes) * 2 * uint64_t(p->model->cfg.n_layers) / 16;
+}
+
 NMX_API nmx_status_t nmx_kv_pool_destroy(nmx_kv_pool_t pool) {
   API_BEGIN;
   if (!pool) return NMX_OK;

@@ -1,21 +1,17 @@
-// Attention over the paged KV pool (GQA, causal), plus the reference's
-// quantized-KV single-query kernel restated for sm_100a.
+// The paged-attention dispatcher, RoPE + KV append for prefill rows (f16 or
+// quantized pages), and the reference's quantized-KV single-query kernel
+// restated for sm_100a. The paged decode kernel itself is in
+// attention_mma.cu, the prefill kernels in attention_prefill.cu and
+// attention_prefill_tc.cu.
 //
-// Paged layout per layer: K[num_blocks][Hkv][BT][D], V likewise, fp16. A
-// CTA owns (query row, kv head, key split) and serves every q head of the
-// GQA group, so each K/V block is read once per kv head. Long contexts are
-// split over several CTAs whose partial (o, max, sum) are combined by the
-// last CTA to finish (an atomic ticket per (row, kv head), reset by that
-// CTA), which needs no grid-wide wait.
-//
-// The decode variant (FUSED) also applies RoPE to q and to the new key and
-// appends the new k/v to its page: the CTA whose split contains the new
-// position writes them before it reads the block, so the KV append and the
-// attention are one launch. Replaces MLXFast.scaledDotProductAttention over
-// KVCacheSimple (mlx-swift-lm; reached from
+// Paged layout per layer: K[num_blocks][Hkv][BT][D], V likewise, fp16; or,
+// for a quantized pool, one page record per (block, kv head) of K and of V
+// (kv_page_bytes). Replaces MLXFast.scaledDotProductAttention over
+// KVCacheSimple / the quantized KV cache (mlx-swift-lm; reached from
 // Sources/NovaMLXEngine/FusedBatchScheduler.swift:1215) and the separate
 // KVCache.update of the reference's batched decode
 // (Sources/NovaMLXEngine/FusedBatchDecode.swift:7-147).
+#include "attn_common.cuh"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -64,6 +60,54 @@ __global__ void __launch_bounds__(128) rope_append_kernel(half* qkv, long ldq, i
     const int kh = i / D, d = i % D;
     const long slot = ((slot0 + kh) * BT + pos % BT) * D;
     Vc[slot + d] = r[(Hq + Hkv + kh) * D + d];
+  }
+  grid_launch_dependents();
+}
+
+// The same RoPE for q, with K and V appended to quantized page records: the
+// CTA's warps take (k | v, kv head) rows; a row is roped (k), rounded to f16
+// and quantized by the warp (quantize_row_warp) into its slot.
+template <int D>
+__global__ void __launch_bounds__(128) rope_append_q_kernel(half* qkv, long ldq, int Hq, int Hkv,
+                                                            const int* tok_seq, const int* tok_pos,
+                                                            const int* block_tables, int max_blocks, int BT,
+                                                            unsigned char* Kc, unsigned char* Vc, int bits, int gs,
+                                                            const float* inv_freq, half* q_out, long ldqo) {
+  grid_wait();
+  constexpr int VPL = D / 32;
+  const int row = blockIdx.x;
+  const int seq = tok_seq[row], pos = tok_pos[row];
+  const half* r = qkv + long(row) * ldq;
+  half* qo = q_out + long(row) * ldqo;
+  for (int i = threadIdx.x; i < Hq * (D / 2); i += blockDim.x) {
+    const int hh = i / (D / 2), d = i % (D / 2);
+    float r0, r1;
+    const half* src = r + hh * D;
+    rope_pair(__half2float(src[d]), __half2float(src[d + D / 2]), float(pos) * inv_freq[d], r0, r1);
+    qo[hh * D + d] = __float2half_rn(r0);
+    qo[hh * D + d + D / 2] = __float2half_rn(r1);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long blk = block_tables[long(seq) * max_blocks + pos / BT];
+  const int pq = 16 * (D * bits / 8 + 2 * (D / gs) * 2);
+  for (int it = warp; it < 2 * Hkv; it += blockDim.x / 32) {
+    const int kind = it / Hkv, kh = it % Hkv;
+    const half* src = r + (Hq + kind * Hkv + kh) * D;
+    float v[VPL];
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int d = lane * VPL + i;
+      if (kind == 0) {
+        const int d0 = d < D / 2 ? d : d - D / 2;
+        float r0, r1;
+        rope_pair(__half2float(src[d0]), __half2float(src[d0 + D / 2]), float(pos) * inv_freq[d0], r0, r1);
+        v[i] = __half2float(__float2half_rn(d < D / 2 ? r0 : r1));
+      } else {
+        v[i] = __half2float(src[d]);
+      }
+    }
+    unsigned char* rec = (kind == 0 ? Kc : Vc) + (blk * Hkv + kh) * pq;
+    quantize_row_warp<D>(v, bits, gs, rec, pos % BT);
   }
   grid_launch_dependents();
 }
@@ -156,9 +200,24 @@ nmx_status_t paged_attention(Ctx* c, const AttnArgs& a, bool fused) {
 nmx_status_t rope_append(Ctx* c, void* qkv, long ldq, int T, int Hq, int Hkv, int D,
                          const int* tok_seq, const int* tok_pos, const int* block_tables,
                          int max_blocks, int BT, void* k_cache, void* v_cache,
-                         const float* inv_freq, void* q_out, long ldqo) {
+                         const float* inv_freq, void* q_out, long ldqo, int kv_bits, int kv_gs) {
   if (T == 0) return NMX_OK;
   auto* q = reinterpret_cast<half*>(qkv);
+  if (kv_bits != 0) {
+    NMX_CHECK((kv_bits == 4 || kv_bits == 8) && (kv_gs == 32 || kv_gs == 64), NMX_ERR_UNSUPPORTED,
+              "rope_append: quantized pages need 4 or 8 bits, group 32 or 64");
+    auto* kc = reinterpret_cast<unsigned char*>(k_cache);
+    auto* vc = reinterpret_cast<unsigned char*>(v_cache);
+    if (D == 128)
+      return launch(c, rope_append_q_kernel<128>, dim3(T), dim3(128), 0, q, ldq, Hq, Hkv, tok_seq, tok_pos,
+                    block_tables, max_blocks, BT, kc, vc, kv_bits, kv_gs, inv_freq,
+                    reinterpret_cast<half*>(q_out), ldqo);
+    if (D == 64)
+      return launch(c, rope_append_q_kernel<64>, dim3(T), dim3(128), 0, q, ldq, Hq, Hkv, tok_seq, tok_pos,
+                    block_tables, max_blocks, BT, kc, vc, kv_bits, kv_gs, inv_freq,
+                    reinterpret_cast<half*>(q_out), ldqo);
+    NMX_CHECK(false, NMX_ERR_UNSUPPORTED, "rope_append: head_dim must be 64 or 128");
+  }
   if (D == 128)
     return launch(c, rope_append_kernel<128>, dim3(T), dim3(128), 0, q, ldq, Hq, Hkv, tok_seq,
                   tok_pos, block_tables, max_blocks, BT, reinterpret_cast<half*>(k_cache),

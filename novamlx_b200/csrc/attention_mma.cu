@@ -62,7 +62,18 @@ __device__ __forceinline__ void st_dsmem(void* p, unsigned rank, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
 }
 
-template <int D, bool FUSED>
+// KQ = 0: f16 pages. KQ = 4 / 8: quantized pages (kv_page_bytes): each warp
+// copies a block's K and V page records into its ring, dequantizes them into
+// its own swizzled f16 tiles right before use, and the MMA path is the same.
+template <int D, int KQ>
+struct DecodeSmem {
+  static constexpr int TILE = 16 * D * 2;
+  static constexpr int PQ = KQ ? kv_page_bytes(D, KQ, 32) : TILE;  // the largest record (group 32)
+  static constexpr int WARP = KQ ? kAStages * 2 * PQ + 2 * TILE : kAStages * 2 * TILE;
+  static constexpr size_t BYTES = TILE + size_t(kAW) * WARP;
+};
+
+template <int D, bool FUSED, int KQ>
 __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) {
   constexpr int BT = 16;
   constexpr int CH = D / 8;          // 16-byte chunks per row
@@ -70,9 +81,12 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
   constexpr int KSTEPS = D / 16;
   constexpr int NT = D / 8;
   constexpr float kLog2e = 1.4426950408889634f;
+  using SM = DecodeSmem<D, KQ>;
   extern __shared__ __align__(128) unsigned char sm[];
   unsigned char* q_sm = sm;
   unsigned char* ring_all = sm + TILE;
+  // bytes of one page record (K or V of one block and kv head)
+  const int pq = KQ ? kv_page_bytes(D, KQ, a.kv_gs) : TILE;
   // per-warp softmax states; entry kAW is the new token (FUSED, owner split)
   __shared__ float s_m[kAW + 1][kMaxRepA], s_l[kAW + 1][kMaxRepA];
   __shared__ float c_ml[kMaxRepA][2];  // this split's (max, denominator) per q head
@@ -107,19 +121,34 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
     b1 = min(nblk, b0 + bps);
     bt = a.block_tables + long(seq) * a.max_blocks;
   };
-  unsigned char* ring = ring_all + warp * (kAStages * 2 * TILE);
+  unsigned char* ring = ring_all + warp * SM::WARP;
+  // quantized pages: this warp's dequantized f16 K and V tiles
+  unsigned char* kdq = ring + kAStages * 2 * SM::PQ;
+  unsigned char* vdq = kdq + TILE;
   auto issue = [&](int stage, int b) {
     if (b < b1) {
-      const long base = (long(bt[b]) * Hkv + h) * BT * D;  // halves
-      const unsigned char* ks = reinterpret_cast<const unsigned char*>(Kc + base);
-      const unsigned char* vs = reinterpret_cast<const unsigned char*>(Vc + base);
-      unsigned char* kd = ring + stage * 2 * TILE;
-      unsigned char* vd = kd + TILE;
+      if constexpr (KQ == 0) {
+        const long base = (long(bt[b]) * Hkv + h) * BT * D;  // halves
+        const unsigned char* ks = reinterpret_cast<const unsigned char*>(Kc + base);
+        const unsigned char* vs = reinterpret_cast<const unsigned char*>(Vc + base);
+        unsigned char* kd = ring + stage * 2 * TILE;
+        unsigned char* vd = kd + TILE;
 #pragma unroll
-      for (int i = lane; i < BT * CH; i += 32) {
-        const int r = i / CH, c = i % CH;
-        cp_async16a(kd + swz<D>(r, c), ks + i * 16);
-        cp_async16a(vd + swz<D>(r, c), vs + i * 16);
+        for (int i = lane; i < BT * CH; i += 32) {
+          const int r = i / CH, c = i % CH;
+          cp_async16a(kd + swz<D>(r, c), ks + i * 16);
+          cp_async16a(vd + swz<D>(r, c), vs + i * 16);
+        }
+      } else {
+        const long base = (long(bt[b]) * Hkv + h) * pq;  // bytes
+        const unsigned char* ks = reinterpret_cast<const unsigned char*>(Kc) + base;
+        const unsigned char* vs = reinterpret_cast<const unsigned char*>(Vc) + base;
+        unsigned char* kd = ring + stage * 2 * SM::PQ;
+        unsigned char* vd = kd + SM::PQ;
+        for (int i = lane; i < pq / 16; i += 32) {
+          cp_async16a(kd + i * 16, ks + i * 16);
+          cp_async16a(vd + i * 16, vs + i * 16);
+        }
       }
     }
     cp_commit();
@@ -161,21 +190,47 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
     if (owner) {
       // the new token: roped k and v to its page (for later steps) and to
       // shared memory (for this one)
-      const long slot = (long(bt[bpos]) * Hkv + h) * BT + pos % BT;
       const half* kr = Q + (Hq + h) * D;
       const half* vr = Q + (Hq + Hkv + h) * D;
-      for (int d = tid; d < D / 2; d += kAW * 32) {
-        float r0, r1;
-        rope2(__half2float(kr[d]), __half2float(kr[d + D / 2]), float(pos) * a.inv_freq[d], r0, r1);
-        const half k0 = __float2half_rn(r0), k1 = __float2half_rn(r1);
-        Kc[slot * D + d] = k0;
-        Kc[slot * D + d + D / 2] = k1;
-        s_knew[d] = k0;
-        s_knew[d + D / 2] = k1;
-      }
-      for (int d = tid; d < D; d += kAW * 32) {
-        Vc[slot * D + d] = vr[d];
-        s_vnew[d] = vr[d];
+      if constexpr (KQ == 0) {
+        const long slot = (long(bt[bpos]) * Hkv + h) * BT + pos % BT;
+        for (int d = tid; d < D / 2; d += kAW * 32) {
+          float r0, r1;
+          rope2(__half2float(kr[d]), __half2float(kr[d + D / 2]), float(pos) * a.inv_freq[d], r0, r1);
+          const half k0 = __float2half_rn(r0), k1 = __float2half_rn(r1);
+          Kc[slot * D + d] = k0;
+          Kc[slot * D + d + D / 2] = k1;
+          s_knew[d] = k0;
+          s_knew[d + D / 2] = k1;
+        }
+        for (int d = tid; d < D; d += kAW * 32) {
+          Vc[slot * D + d] = vr[d];
+          s_vnew[d] = vr[d];
+        }
+      } else if (warp < 2) {
+        // warp 0: k (roped, rounded to f16), warp 1: v; quantized into the
+        // page record, and the dequantized values are what this step uses
+        // (the cache holds nothing finer)
+        constexpr int VPL = D / 32;
+        const long rec = (long(bt[bpos]) * Hkv + h) * pq;
+        float v[VPL];
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+          const int d = lane * VPL + i;
+          if (warp == 0) {
+            const int d0 = d < D / 2 ? d : d - D / 2;
+            float r0, r1;
+            rope2(__half2float(kr[d0]), __half2float(kr[d0 + D / 2]), float(pos) * a.inv_freq[d0], r0, r1);
+            v[i] = __half2float(__float2half_rn(d < D / 2 ? r0 : r1));
+          } else {
+            v[i] = __half2float(vr[d]);
+          }
+        }
+        unsigned char* page = reinterpret_cast<unsigned char*>(warp == 0 ? a.k_cache : a.v_cache) + rec;
+        quantize_row_warp<D>(v, KQ, a.kv_gs, page, pos % BT);
+        half* dst = warp == 0 ? s_knew : s_vnew;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) dst[lane * VPL + i] = __float2half_rn(v[i]);
       }
     }
   } else {
@@ -209,6 +264,14 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
     __syncwarp();
     const unsigned char* kt = ring + stage * 2 * TILE;
     const unsigned char* vt = kt + TILE;
+    if constexpr (KQ != 0) {
+      const unsigned char* kraw = ring + stage * 2 * SM::PQ;
+      dequant_page_warp<D>(kraw, KQ, a.kv_gs, kdq);
+      dequant_page_warp<D>(kraw + SM::PQ, KQ, a.kv_gs, vdq);
+      __syncwarp();
+      kt = kdq;
+      vt = vdq;
+    }
     float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
     for (int kk = 0; kk < KSTEPS; ++kk) {
@@ -388,11 +451,10 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
   // no remote access follows phase 2: a CTA may leave
 }
 
-template <int D, bool FUSED>
+template <int D, bool FUSED, int KQ>
 nmx_status_t launch_mma(Ctx* c, const AttnArgs& a, int S) {
-  constexpr int TILE = 16 * D * 2;
-  const size_t smem = TILE + size_t(kAW) * kAStages * 2 * TILE;
-  auto kern = paged_decode_mma_kernel<D, FUSED>;
+  const size_t smem = DecodeSmem<D, KQ>::BYTES;
+  auto kern = paged_decode_mma_kernel<D, FUSED, KQ>;
   static std::mutex mu;
   static std::map<int, bool> attr;  // per device
   {
@@ -441,8 +503,21 @@ nmx_status_t paged_attention_mma(Ctx* c, const AttnArgs& a, bool fused) {
   NMX_CHECK(a.splits >= 1, NMX_ERR_UNSUPPORTED, "paged attention: splits >= 1");
   // the splits of one (row, kv head) form a cluster: at most 16 CTAs
   const int S = std::min(a.splits, kMaxClusterA);
-  if (a.D == 128) return fused ? launch_mma<128, true>(c, a, S) : launch_mma<128, false>(c, a, S);
-  if (a.D == 64) return fused ? launch_mma<64, true>(c, a, S) : launch_mma<64, false>(c, a, S);
+  NMX_CHECK(a.kv_bits == 0 || ((a.kv_bits == 4 || a.kv_bits == 8) && (a.kv_gs == 32 || a.kv_gs == 64)),
+            NMX_ERR_UNSUPPORTED, "paged attention: quantized pages need 4 or 8 bits, group 32 or 64");
+#define NMX_DEC(DD, KQ) \
+  return fused ? launch_mma<DD, true, KQ>(c, a, S) : launch_mma<DD, false, KQ>(c, a, S)
+  if (a.D == 128) {
+    if (a.kv_bits == 4) NMX_DEC(128, 4);
+    if (a.kv_bits == 8) NMX_DEC(128, 8);
+    NMX_DEC(128, 0);
+  }
+  if (a.D == 64) {
+    if (a.kv_bits == 4) NMX_DEC(64, 4);
+    if (a.kv_bits == 8) NMX_DEC(64, 8);
+    NMX_DEC(64, 0);
+  }
+#undef NMX_DEC
   NMX_CHECK(false, NMX_ERR_UNSUPPORTED, "paged attention: head_dim must be 64 or 128");
 }
 

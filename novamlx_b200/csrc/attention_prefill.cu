@@ -33,7 +33,18 @@ constexpr int kPQB = 16;      // query rows per work item
 constexpr int kPStages = 3;   // K/V ring stages
 constexpr int kPMaxRep = 8;   // q heads per kv head (one warp each)
 
-template <int D>
+// KQ = 0: f16 pages; 4 / 8: quantized page records (kv_page_bytes) copied
+// into the ring and dequantized by the CTA into one shared K/V tile pair per
+// block before the warps read it.
+template <int D, int KQ>
+struct PrefillSmem {
+  static constexpr int TILE = 16 * D * 2;
+  static constexpr int PQ = KQ ? kv_page_bytes(D, KQ, 32) : TILE;  // the largest record (group 32)
+  static constexpr size_t BYTES =
+      size_t(kPMaxRep) * TILE + size_t(kPStages) * 2 * PQ + (KQ ? 2 * size_t(TILE) : 0);
+};
+
+template <int D, int KQ>
 __global__ void __launch_bounds__(kPMaxRep * 32) paged_prefill_mma_kernel(AttnArgs a, const int2* items) {
   constexpr int BT = 16;
   constexpr int CH = D / 8;          // 16-byte chunks per row
@@ -53,8 +64,12 @@ __global__ void __launch_bounds__(kPMaxRep * 32) paged_prefill_mma_kernel(AttnAr
   const int nthr = rep * 32;
   half* Kc = reinterpret_cast<half*>(a.k_cache);
   half* Vc = reinterpret_cast<half*>(a.v_cache);
+  using PS = PrefillSmem<D, KQ>;
   unsigned char* q_sm = sm;                         // [rep][16][D] swizzled
   unsigned char* ring = sm + size_t(kPMaxRep) * TILE;  // [stage][K | V]
+  unsigned char* kdq = ring + size_t(kPStages) * 2 * PS::PQ;  // quantized pages: the block's f16 K, V
+  unsigned char* vdq = kdq + TILE;
+  const int pq = KQ ? kv_page_bytes(D, KQ, a.kv_gs) : TILE;
 
   grid_wait();  // q rows and the pages (RoPE + append) come from the kernels before
   if (tid < kPQB) s_pos[tid] = tid < nr ? a.tok_pos[r0 + tid] : -1;
@@ -65,15 +80,27 @@ __global__ void __launch_bounds__(kPMaxRep * 32) paged_prefill_mma_kernel(AttnAr
 
   auto issue = [&](int stage, int b) {
     if (b < nblk) {
-      const long base = (long(bt[b]) * Hkv + h) * BT * D;  // halves
-      const unsigned char* ks = reinterpret_cast<const unsigned char*>(Kc + base);
-      const unsigned char* vs = reinterpret_cast<const unsigned char*>(Vc + base);
-      unsigned char* kd = ring + stage * 2 * TILE;
-      unsigned char* vd = kd + TILE;
-      for (int i = tid; i < BT * CH; i += nthr) {
-        const int r = i / CH, c = i % CH;
-        cp_async16a(kd + swz<D>(r, c), ks + i * 16);
-        cp_async16a(vd + swz<D>(r, c), vs + i * 16);
+      if constexpr (KQ == 0) {
+        const long base = (long(bt[b]) * Hkv + h) * BT * D;  // halves
+        const unsigned char* ks = reinterpret_cast<const unsigned char*>(Kc + base);
+        const unsigned char* vs = reinterpret_cast<const unsigned char*>(Vc + base);
+        unsigned char* kd = ring + stage * 2 * TILE;
+        unsigned char* vd = kd + TILE;
+        for (int i = tid; i < BT * CH; i += nthr) {
+          const int r = i / CH, c = i % CH;
+          cp_async16a(kd + swz<D>(r, c), ks + i * 16);
+          cp_async16a(vd + swz<D>(r, c), vs + i * 16);
+        }
+      } else {
+        const long base = (long(bt[b]) * Hkv + h) * pq;  // bytes
+        const unsigned char* ks = reinterpret_cast<const unsigned char*>(Kc) + base;
+        const unsigned char* vs = reinterpret_cast<const unsigned char*>(Vc) + base;
+        unsigned char* kd = ring + stage * 2 * PS::PQ;
+        unsigned char* vd = kd + PS::PQ;
+        for (int i = tid; i < pq / 16; i += nthr) {
+          cp_async16a(kd + i * 16, ks + i * 16);
+          cp_async16a(vd + i * 16, vs + i * 16);
+        }
       }
     }
     cp_commit();
@@ -117,6 +144,14 @@ __global__ void __launch_bounds__(kPMaxRep * 32) paged_prefill_mma_kernel(AttnAr
     __syncthreads();
     const unsigned char* kt = ring + (b % kPStages) * 2 * TILE;
     const unsigned char* vt = kt + TILE;
+    if constexpr (KQ != 0) {
+      const unsigned char* kraw = ring + (b % kPStages) * 2 * PS::PQ;
+      dequant_page<D>(kraw, KQ, a.kv_gs, kdq, tid, nthr);
+      dequant_page<D>(kraw + PS::PQ, KQ, a.kv_gs, vdq, tid, nthr);
+      __syncthreads();
+      kt = kdq;
+      vt = vdq;
+    }
     float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
     for (int kk = 0; kk < KSTEPS; ++kk) {
@@ -201,21 +236,28 @@ __global__ void __launch_bounds__(kPMaxRep * 32) paged_prefill_mma_kernel(AttnAr
   }
 }
 
-template <int D>
+template <int D, int KQ>
 nmx_status_t launch_prefill(Ctx* c, const AttnArgs& a, const int2* items, int n_items) {
   const int rep = a.Hq / a.Hkv;
-  const size_t smem = size_t(kPMaxRep) * 16 * D * 2 + size_t(kPStages) * 2 * 16 * D * 2;
+  const size_t smem = PrefillSmem<D, KQ>::BYTES;
+  auto kern = paged_prefill_mma_kernel<D, KQ>;
   static std::mutex mu;
   static std::map<int, bool> set;
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!set[c->device]) {
-      NMX_CUDA_OK(cudaFuncSetAttribute(paged_prefill_mma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       int(smem)));
+      NMX_CUDA_OK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
       set[c->device] = true;
     }
   }
-  return launch(c, paged_prefill_mma_kernel<D>, dim3(n_items, a.Hkv), dim3(rep * 32), smem, a, items);
+  return launch(c, kern, dim3(n_items, a.Hkv), dim3(rep * 32), smem, a, items);
+}
+
+template <int D>
+nmx_status_t launch_prefill_q(Ctx* c, const AttnArgs& a, const int2* items, int n_items) {
+  if (a.kv_bits == 4) return launch_prefill<D, 4>(c, a, items, n_items);
+  if (a.kv_bits == 8) return launch_prefill<D, 8>(c, a, items, n_items);
+  return launch_prefill<D, 0>(c, a, items, n_items);
 }
 
 }  // namespace
@@ -246,13 +288,17 @@ nmx_status_t paged_prefill_attention(Ctx* c, const AttnArgs& a, const int2* item
   NMX_CHECK(a.Hkv > 0 && a.Hq % a.Hkv == 0 && a.Hq / a.Hkv <= kPMaxRep, NMX_ERR_UNSUPPORTED,
             "prefill attention: q heads per kv head must be <= 8");
   if (n_items == 0) return NMX_OK;
+  NMX_CHECK(a.kv_bits == 0 || ((a.kv_bits == 4 || a.kv_bits == 8) && (a.kv_gs == 32 || a.kv_gs == 64)),
+            NMX_ERR_UNSUPPORTED, "prefill attention: quantized pages need 4 or 8 bits, group 32 or 64");
+  NMX_CHECK(a.kv_bits == 0 || a.prefill_tc_items == 0, NMX_ERR_INVALID,
+            "prefill attention: quantized pages go through the small-item kernel");
   const int n_tc = std::min(a.prefill_tc_items, n_items);
   if (n_tc > 0) NMX_TRY(paged_prefill_attention_tc(c, a, items, n_tc));
   if (n_tc == n_items) return NMX_OK;
   items += n_tc;
   n_items -= n_tc;
-  if (a.D == 128) return launch_prefill<128>(c, a, items, n_items);
-  if (a.D == 64) return launch_prefill<64>(c, a, items, n_items);
+  if (a.D == 128) return launch_prefill_q<128>(c, a, items, n_items);
+  if (a.D == 64) return launch_prefill_q<64>(c, a, items, n_items);
   NMX_CHECK(false, NMX_ERR_UNSUPPORTED, "prefill attention: head_dim must be 64 or 128");
 }
 

@@ -63,13 +63,8 @@ __device__ __forceinline__ void rope2(float a, float b, float ang, float& ra, fl
 }
 
 // ---------------------------------------------------------------------------
-// Quantized KV pages (the kvBits path). A page record holds one (block, kv
-// head) of K or V for 16 tokens: codes [16][D * bits / 32] u32 (MLX packing,
-// low bits first along d), then scales [16][D / gs] and biases [16][D / gs]
-// f16 — MLX-affine quantization in groups of gs along head_dim.
-__host__ __device__ constexpr int kv_page_bytes(int D, int bits, int gs) {
-  return bits == 0 ? 16 * D * 2 : 16 * (D * bits / 8 + 2 * (D / gs) * 2);
-}
+// Quantized KV pages (the kvBits path): page records as kv_page_bytes
+// (kernels.h) describes them.
 
 // One K or V row held by a warp (lane l: values d = l * VPL .. + VPL - 1),
 // quantized in groups of gs: scale = (max - min) / (2^bits - 1) and bias =
@@ -150,16 +145,17 @@ __device__ __forceinline__ uint4 dq8_chunk(uint2 w, __half2 s2, __half2 b2) {
   return make_uint4(r[0], r[1], r[2], r[3]);
 }
 
-// One page record dequantized by a warp into a swizzled [16][D] f16 tile.
+// One page record dequantized into a swizzled [16][D] f16 tile by the
+// threads i0, i0 + stride, ... (a warp: lane, 32; a CTA: tid, blockDim).
 template <int D>
-__device__ __forceinline__ void dequant_page_warp(const unsigned char* rec, int bits, int gs, unsigned char* tile) {
+__device__ __forceinline__ void dequant_page(const unsigned char* rec, int bits, int gs, unsigned char* tile, int i0,
+                                             int stride) {
   constexpr int CH = D / 8;
-  const int lane = threadIdx.x & 31;
   const int rowbytes = D * bits / 8, ng = D / gs;
   const half* sc = reinterpret_cast<const half*>(rec + 16 * rowbytes);
   const half* bi = sc + 16 * ng;
 #pragma unroll 4
-  for (int i = lane; i < 16 * CH; i += 32) {
+  for (int i = i0; i < 16 * CH; i += stride) {
     const int r = i / CH, c = i % CH;
     const int g = (8 * c) / gs;
     const __half2 s2 = __half2half2(sc[r * ng + g]), b2 = __half2half2(bi[r * ng + g]);
@@ -167,6 +163,10 @@ __device__ __forceinline__ void dequant_page_warp(const unsigned char* rec, int 
                               : dq8_chunk(*reinterpret_cast<const uint2*>(rec + r * rowbytes + 8 * c), s2, b2);
     *reinterpret_cast<uint4*>(tile + swz<D>(r, c)) = o;
   }
+}
+template <int D>
+__device__ __forceinline__ void dequant_page_warp(const unsigned char* rec, int bits, int gs, unsigned char* tile) {
+  dequant_page<D>(rec, bits, gs, tile, threadIdx.x & 31, 32);
 }
 
 }  // namespace

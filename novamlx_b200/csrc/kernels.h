@@ -114,6 +114,14 @@ nmx_status_t unpack_from_records(Ctx* c, const void* rec, int rows, int K, long 
                                  void* b, int part_mask);
 
 // ---- attention
+// A KV page record: one (block, kv head) of K or V for 16 tokens. f16 pages
+// (bits = 0): [16][D] f16. Quantized pages: codes [16][D * bits / 32] u32
+// (MLX packing, low bits first along d), then scales [16][D / gs] and biases
+// [16][D / gs] f16 — MLX-affine quantization in groups of gs along head_dim.
+__host__ __device__ constexpr int kv_page_bytes(int D, int bits, int gs) {
+  return bits == 0 ? 16 * D * 2 : 16 * (D * bits / 8 + 2 * (D / gs) * 2);
+}
+
 struct AttnArgs {
   const void* q = nullptr;     // FUSED: qkv rows [T, ldq] (pre-RoPE q|k|v); else q [T, Hq*D] roped
   long ldq = 0;
@@ -136,6 +144,9 @@ struct AttnArgs {
   int pool_blocks = 0;
   int prefill_tc_items = 0;
   unsigned* err = nullptr;
+  // quantized pages (kv_page_bytes): code width 4 / 8 and group along the
+  // head dim; 0 = f16 pages
+  int kv_bits = 0, kv_gs = 0;
 };
 
 // fused = 1: apply RoPE to q and append the row's own k/v (one query row per
@@ -174,7 +185,7 @@ nmx_status_t paged_attention_mma(Ctx* c, const AttnArgs& a, bool fused);
 nmx_status_t rope_append(Ctx* c, void* qkv, long ldq, int T, int Hq, int Hkv, int D,
                          const int* tok_seq, const int* tok_pos, const int* block_tables,
                          int max_blocks, int BT, void* k_cache, void* v_cache,
-                         const float* inv_freq, void* q_out, long ldqo);
+                         const float* inv_freq, void* q_out, long ldqo, int kv_bits = 0, int kv_gs = 0);
 
 nmx_status_t quantized_sdpa(Ctx* c, const void* q, const uint32_t* kw, const void* ks,
                             const void* kb, const uint32_t* vw, const void* vs, const void* vb,

@@ -472,13 +472,19 @@ nmx_status_t Model::get_tensor(const std::string& name, void* host, size_t host_
 
 // ------------------------------------------------------------------ KV pool
 
-nmx_status_t KvPool::create(Model* m, int block_tokens, int num_blocks, KvPool** out) {
+nmx_status_t KvPool::create(Model* m, int block_tokens, int num_blocks, KvPool** out, int kv_bits, int kv_gs) {
   NMX_CHECK(block_tokens == kBT, NMX_ERR_UNSUPPORTED, "kv pool: block size must be 16 tokens");
   NMX_CHECK(num_blocks > 0, NMX_ERR_INVALID, "kv pool: num_blocks must be positive");
+  const int D = m->cfg.head_dim;
+  NMX_CHECK(kv_bits == 0 || ((kv_bits == 4 || kv_bits == 8) && (kv_gs == 32 || kv_gs == 64) &&
+                             (D == 64 || D == 128)),
+            NMX_ERR_UNSUPPORTED, "kv pool: quantized pages need 4 or 8 bits, group 32 or 64, head_dim 64 or 128");
   auto* p = new KvPool();
   p->model = m;
   p->num_blocks = num_blocks;
-  p->block_bytes = size_t(m->cfg.n_kv_heads) * kBT * m->cfg.head_dim * 2;
+  p->kv_bits = kv_bits;
+  p->kv_gs = kv_bits ? kv_gs : 0;
+  p->block_bytes = size_t(m->cfg.n_kv_heads) * size_t(kv_page_bytes(D, kv_bits, kv_gs));
   p->layer_stride = 2 * p->block_bytes * size_t(num_blocks);
   const size_t total = p->layer_stride * m->cfg.n_layers;
   nmx_status_t st = alloc_dev(reinterpret_cast<void**>(&p->base), total);
@@ -592,6 +598,7 @@ nmx_status_t Model::run_layers_decode(KvPool* pool, int B) {
     at.T = B; at.Hq = cf.n_heads; at.Hkv = cf.n_kv_heads; at.D = cf.head_dim; at.BT = kBT;
     at.splits = splits; at.scale = 1.0f / std::sqrt(float(cf.head_dim));
     at.kv_static = true;
+    at.kv_bits = pool->kv_bits; at.kv_gs = pool->kv_gs;
     NMX_TRY(paged_attention(c, at, true));
 
     NMX_TRY(block_out(ly.o, attn, Nq, B, 0));
@@ -613,7 +620,7 @@ nmx_status_t Model::run_layers_prefill(KvPool* pool, int T) {
     NMX_TRY(linear(ly.qkv, h, H, ly.attn_norm, T, Nqkv, 0, ly.qkv_bias, qkv, Nqkv, nullptr, 0, EPI_STORE));
     NMX_TRY(rope_append(c, qkv, Nqkv, T, cf.n_heads, cf.n_kv_heads, cf.head_dim, tok_seq, tok_pos,
                         block_tables, kBlockCap, kBT, pool->k_layer(l), pool->v_layer(l), inv_freq,
-                        q_roped, Nq));
+                        q_roped, Nq, pool->kv_bits, pool->kv_gs));
     AttnArgs at;
     at.q = q_roped; at.ldq = Nq;
     at.k_cache = pool->k_layer(l); at.v_cache = pool->v_layer(l);
@@ -622,6 +629,7 @@ nmx_status_t Model::run_layers_prefill(KvPool* pool, int T) {
     at.T = T; at.Hq = cf.n_heads; at.Hkv = cf.n_kv_heads; at.D = cf.head_dim; at.BT = kBT;
     at.splits = 1; at.scale = 1.0f / std::sqrt(float(cf.head_dim));
     at.pool_blocks = pool->num_blocks; at.prefill_tc_items = n_pf_tc; at.err = c->dev_err;
+    at.kv_bits = pool->kv_bits; at.kv_gs = pool->kv_gs;
     NMX_TRY(paged_prefill_attention(c, at, pf_items, n_pf_items));
 
     NMX_TRY(block_out(ly.o, attn, Nq, T, 0));
@@ -707,7 +715,7 @@ nmx_status_t Model::run_decode_graph(KvPool* pool, int B) {
   return NMX_OK;
 }
 
-nmx_status_t Model::upload_batch(const nmx_seq_t* seqs, int n, int* T_out, bool* decode_out) {
+nmx_status_t Model::upload_batch(const nmx_seq_t* seqs, int n, int* T_out, bool* decode_out, bool tc_items) {
   NMX_CHECK(n > 0 && seqs, NMX_ERR_INVALID, "forward: empty batch");
   NMX_CHECK(n <= max_batch, NMX_ERR_INVALID, "forward: more sequences than max_batch");
   int T = 0;
@@ -760,7 +768,8 @@ nmx_status_t Model::upload_batch(const nmx_seq_t* seqs, int n, int* T_out, bool*
   n_pf_tc = 0;
   if (!decode) {
     int2* items = reinterpret_cast<int2*>(tbl + size_t(max_batch) * kBlockCap);
-    n_pf_items = prefill_items(sq, T, cfg.head_dim, cfg.n_heads / cfg.n_kv_heads, items, &n_pf_tc);
+    // quantized pages go through the small-item kernel only
+    n_pf_items = prefill_items(sq, T, tc_items ? cfg.head_dim : 0, cfg.n_heads / cfg.n_kv_heads, items, &n_pf_tc);
     NMX_CUDA_OK(cudaMemcpyAsync(pf_items, items, size_t(n_pf_items) * 8, cudaMemcpyHostToDevice, c->stream));
     h2d_bytes_last += size_t(n_pf_items) * 8;
   }
@@ -777,7 +786,7 @@ nmx_status_t Model::forward(KvPool* pool, const nmx_seq_t* seqs, int n, nmx_out_
   pool_blocks_hint = pool->num_blocks;
   int T = 0;
   bool decode = false;
-  NMX_TRY(upload_batch(seqs, n, &T, &decode));
+  NMX_TRY(upload_batch(seqs, n, &T, &decode, pool->kv_bits == 0));
   const bool all = (mode == NMX_OUT_ARGMAX_ALL || mode == NMX_OUT_LOGITS_ALL);
   const bool logits = (mode == NMX_OUT_LOGITS_LAST || mode == NMX_OUT_LOGITS_ALL);
   const int rows = all ? T : n;

@@ -111,7 +111,7 @@ struct Model {
   nmx_status_t run_head(const void* x, int rows, bool want_logits, int* next_tokens);
   nmx_status_t decode_step_body(KvPool* pool, int B);
   nmx_status_t run_decode_graph(KvPool* pool, int B);
-  nmx_status_t upload_batch(const nmx_seq_t* seqs, int n, int* T_out, bool* decode_out);
+  nmx_status_t upload_batch(const nmx_seq_t* seqs, int n, int* T_out, bool* decode_out, bool tc_items = true);
   nmx_status_t forward(KvPool* pool, const nmx_seq_t* seqs, int n, nmx_out_mode_t mode, void* out_host);
   nmx_status_t finish_step();
   // tensor parallelism: this rank's shard of every linear; o/down partials
@@ -133,11 +133,16 @@ nmx_status_t comm_allreduce_resid(Comm* cm, int region, int rows, int cols, cons
 
 struct KvPool {
   Model* model = nullptr;
-  char* base = nullptr;  // [L][K|V][num_blocks][Hkv][BT][D] f16
+  // [L][K|V][num_blocks][Hkv][BT][D] f16, or for a quantized pool
+  // [L][K|V][num_blocks][Hkv] page records (codes, scales, biases of 16
+  // tokens; kv_page_bytes in attn_common.cuh)
+  char* base = nullptr;
   int num_blocks = 0;
+  int kv_bits = 0, kv_gs = 0;  // 0: f16 pages
   size_t block_bytes = 0;   // one block of K (or V) of one layer
   size_t layer_stride = 0;  // bytes per layer (K and V)
-  static nmx_status_t create(Model* m, int block_tokens, int num_blocks, KvPool** out);
+  static nmx_status_t create(Model* m, int block_tokens, int num_blocks, KvPool** out, int kv_bits = 0,
+                             int kv_gs = 0);
   ~KvPool();
   void* k_layer(int l) const { return base + size_t(l) * layer_stride; }
   void* v_layer(int l) const { return base + size_t(l) * layer_stride + layer_stride / 2; }

@@ -603,6 +603,7 @@ NMX_API nmx_status_t nmx_ssd_save_block(nmx_kv_pool_t pool, int block_id, const 
   nmx::clear_error();
   NMX_CHECK(pool && hash20 && cache_dir, NMX_ERR_INVALID, "nmx_ssd_save_block: null argument");
   nmx::KvPool* p = pool->p;
+  NMX_CHECK(p->kv_bits == 0, NMX_ERR_UNSUPPORTED, "nmx_ssd_save_block: the SSD store holds f16 blocks");
   const nmx_model_cfg& cf = p->model->cfg;
   const int L = cf.n_layers, bt = int(p->block_bytes / (size_t(cf.n_kv_heads) * cf.head_dim * 2));
   std::vector<unsigned char> host(size_t(L) * 2 * p->block_bytes);
@@ -647,6 +648,7 @@ NMX_API nmx_status_t nmx_ssd_load_block(nmx_kv_pool_t pool, const uint8_t hash20
   nmx::clear_error();
   NMX_CHECK(pool && hash20 && cache_dir, NMX_ERR_INVALID, "nmx_ssd_load_block: null argument");
   nmx::KvPool* p = pool->p;
+  NMX_CHECK(p->kv_bits == 0, NMX_ERR_UNSUPPORTED, "nmx_ssd_load_block: the SSD store holds f16 blocks");
   const nmx_model_cfg& cf = p->model->cfg;
   const int L = cf.n_layers;
   const std::string hex = hex20(hash20);

@@ -105,6 +105,8 @@ _proto("nmx_kv_write_blocks", _i, _vp, _ip, _i, _vp)
 _proto("nmx_kv_pool_layer_ptrs", _i, _vp, _i, C.POINTER(_vp), C.POINTER(_vp))
 _proto("nmx_kv_pool_num_blocks", _i, _vp)
 _proto("nmx_kv_pool_fill_random", _i, _vp, _u64, C.c_float)
+_proto("nmx_kv_pool_create_quantized", _i, _vp, _i, _i, _i, _i, C.POINTER(_vp))
+_proto("nmx_kv_pool_bytes_per_token", _u64, _vp)
 _proto("nmx_kv_bytes_per_token", _u64, _vp)
 _proto("nmx_forward", _i, _vp, _vp, C.POINTER(Seq), _i, _i, _vp)
 _proto("nmx_decode_greedy", _i, _vp, _vp, _ip, _ip, _ip, _i, _i, _i, _ip)
@@ -608,15 +610,27 @@ class Model:
 
 
 class KVPool:
-    """nmx_kv_pool_t: fp16 K/V pages of `block_tokens` tokens for every layer."""
+    """nmx_kv_pool_t: K/V pages of `block_tokens` tokens for every layer, fp16 or
+    (kv_bits 4 / 8) MLX-affine quantized in groups of kv_group_size along head_dim."""
 
-    def __init__(self, model: Model, num_blocks: int, block_tokens: int = 16):
+    def __init__(self, model: Model, num_blocks: int, block_tokens: int = 16, kv_bits: int = 0,
+                 kv_group_size: int = 64):
         h = _vp()
-        check(lib.nmx_kv_pool_create(model.h, block_tokens, num_blocks, C.byref(h)))
+        if kv_bits:
+            check(lib.nmx_kv_pool_create_quantized(model.h, block_tokens, num_blocks, kv_bits, kv_group_size,
+                                                   C.byref(h)))
+        else:
+            check(lib.nmx_kv_pool_create(model.h, block_tokens, num_blocks, C.byref(h)))
         self.h = h
         self.model = model
         self.num_blocks = num_blocks
         self.block_tokens = block_tokens
+        self.kv_bits = kv_bits
+        self._gs = kv_group_size
+
+    @property
+    def bytes_per_token(self) -> int:
+        return int(lib.nmx_kv_pool_bytes_per_token(self.h))
 
     def fill_random(self, seed: int = 0, std: float = 1.0):
         """Every page of every layer N(0, std): a cache of a given context without its prefill."""
@@ -628,9 +642,15 @@ class KVPool:
         return k.value, v.value
 
     def read_blocks(self, ids) -> np.ndarray:
-        """Host copy [n, layers, 2, Hkv, block_tokens, head_dim] (raw f16 bits)."""
+        """Host copy [n, layers, 2, Hkv, block_tokens, head_dim] (raw f16 bits);
+        quantized pools: the raw page records [n, layers, 2, block bytes] (uint8)."""
         c = self.model.cfg
         ids = _i32(ids)
+        if self.kv_bits:
+            rec = 16 * (c.head_dim * self.kv_bits // 8 + 2 * (c.head_dim // self._gs) * 2)
+            out = np.empty((len(ids), c.n_layers, 2, c.n_kv_heads * rec), np.uint8)
+            check(lib.nmx_kv_read_blocks(self.h, _iptr(ids), len(ids), out.ctypes.data))
+            return out
         out = np.empty((len(ids), c.n_layers, 2, c.n_kv_heads, self.block_tokens, c.head_dim), np.uint16)
         check(lib.nmx_kv_read_blocks(self.h, _iptr(ids), len(ids), out.ctypes.data))
         return out

@@ -154,3 +154,24 @@ def test_tiny_model_prefix_equals_full():
     rest = m.forward(c2, toks[32:], 32)
     assert np.array_equal(full, rest)
     assert np.array_equal(c1[0][:, :, :40], c2[0][:, :, :40])
+
+
+def test_quantized_kv_cache_oracle():
+    """The oracle's quantized KV cache (quantize on append, read the
+    dequantized values): 8-bit stays close to the f16 cache, 4-bit further
+    away but still close, and the cached rows are exactly representable by
+    their group's codes (at most 2^bits distinct values per group)."""
+    d = dict(vocab=256, hidden=128, n_layers=1, n_heads=4, n_kv_heads=2, head_dim=64, ffn=256, rope_theta=1e4)
+    t = O.random_tensors(O.TinyCfg(**d), seed=4, std=0.05)
+    prompt = np.arange(1, 40) % 256
+    ref = O.OracleModel(O.TinyCfg(**d), t).forward(O.OracleModel(O.TinyCfg(**d), t).new_cache(64), prompt, 0)
+    cos = {}
+    for bits in (8, 4):
+        om = O.OracleModel(O.TinyCfg(**d, kv_bits=bits, kv_group_size=32), t)
+        cache = om.new_cache(64)
+        out = om.forward(cache, prompt, 0)
+        cos[bits] = O.cosine(out, ref)
+        kc = O.f16bits_to_f32(cache[0][0, :, :len(prompt)])  # [Hkv, T, D]
+        for row in kc.reshape(-1, 32):
+            assert len(np.unique(row)) <= 2 ** bits
+    assert cos[8] > 0.9999 and cos[4] > 0.99 and cos[8] >= cos[4]
