@@ -16,13 +16,13 @@ COS_MIN = 0.999
 REL_MAX = 2e-2
 
 
-def check_logits(got, ref) -> float:
+def check_logits(got, ref, rel_max: float = REL_MAX) -> float:
     """Cosine and normwise relative error of every row; returns the largest
     absolute logit error seen."""
     worst = 0.0
     for g, r in zip(np.atleast_2d(got), np.atleast_2d(ref)):
         assert O.cosine(g, r) >= COS_MIN, O.cosine(g, r)
-        assert O.max_rel_err(g, r) <= REL_MAX, O.max_rel_err(g, r)
+        assert O.max_rel_err(g, r) <= rel_max, O.max_rel_err(g, r)
         worst = max(worst, float(np.max(np.abs(np.asarray(g, np.float64) - np.asarray(r, np.float64)))))
     return worst
 
