@@ -456,6 +456,7 @@ NMX_API nmx_status_t nmx_kv_pool_destroy(nmx_kv_pool_t pool) {
   API_BEGIN;
   if (!pool) return NMX_OK;
   cudaStreamSynchronize(pool->p->model->ctx->stream);
+  pool->p->model->graphs_drop_pool(pool->p);
   delete pool->p;
   nmx_model_s* model = pool->model;
   delete pool;

@@ -78,6 +78,19 @@ struct Model {
       if (g.second.exec) cudaGraphExecDestroy(g.second.exec);
     graphs.clear();
   }
+  // the decode graphs captured over `pool` (its pages and page format are
+  // baked in): dropped when the pool goes, since a later pool may get the
+  // same host address
+  void graphs_drop_pool(const void* pool) {
+    for (auto it = graphs.begin(); it != graphs.end();) {
+      if (it->first.second == pool) {
+        if (it->second.exec) cudaGraphExecDestroy(it->second.exec);
+        it = graphs.erase(it);
+      } else {
+        ++it;
+      }
+    }
+  }
 
   // set by resolve() when the named part lives inside decode records
   Lin* rs_lin = nullptr;

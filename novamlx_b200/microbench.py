@@ -1,6 +1,7 @@
 """Per-kernel timings of the decode path, one kernel at a time.
 
   python -m novamlx_b200.microbench gemv [--n 28672] [--k 4096] [--m 1]
+  python -m novamlx_b200.microbench qmm --m 4 --n 4096 --k 4096 --copies 32
   python -m novamlx_b200.microbench gemm [--m 2048] [--n 4096] [--k 4096]
   python -m novamlx_b200.microbench attn [--batch 1] [--ctx 2176]
   python -m novamlx_b200.microbench decode [--layers 2] [--ctx 2048] [--tokens 64] [--batch 1]
@@ -85,6 +86,20 @@ def gemv(ctx, torch, n, k, m, copies, reps):
     us = _time(torch, lambda i: ctx.quantized_matmul_records(x, recs[i % copies], n, out=y), reps)
     nbytes = n * k // 2 + 2 * n * (k // 64) * 2 + m * k * 2 + m * n * 2
     return {"kernel": "qgemv_dl_kernel", "m": m, "n": n, "k": k, "us": round(us, 2), "bytes": nbytes,
+            "gbs": round(nbytes / us / 1e3, 1)}
+
+
+def qmm(ctx, torch, m, n, k, copies, reps):
+    """The operator-level quantized matmul over MLX-layout weights
+    (nmx_op_qmatmul, 4-bit g64, f16) rotating over `copies` weight copies."""
+    wf = torch.randn((n, k), device="cuda", dtype=torch.float32) * 0.02
+    ws = [ctx.quantize(wf, 64, 4) for _ in range(copies)]
+    del wf
+    x = torch.randn((m, k), device="cuda", dtype=torch.float16)
+    y = torch.empty((m, n), device="cuda", dtype=torch.float16)
+    us = _time(torch, lambda i: ctx.quantized_matmul(x, *ws[i % copies], out=y), reps)
+    nbytes = n * k // 2 + 2 * n * (k // 64) * 2 + m * k * 2 + m * n * 2
+    return {"kernel": "qgemv_mlx4_small_kernel", "m": m, "n": n, "k": k, "us": round(us, 2), "bytes": nbytes,
             "gbs": round(nbytes / us / 1e3, 1)}
 
 
@@ -353,7 +368,7 @@ def main():
     from novamlx_b200 import nmx
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemv", "gemm", "attn", "decode", "serve", "spec", "tp"])
+    ap.add_argument("what", choices=["gemv", "qmm", "gemm", "attn", "decode", "serve", "spec", "tp"])
     ap.add_argument("--n", type=int, default=None, help="gemv: 28672, gemm: 4096")
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--m", type=int, default=None, help="gemv: 1, gemm: 2048")
@@ -395,6 +410,8 @@ def main():
     with torch.cuda.stream(c.stream):
         if a.what == "gemv":
             r = gemv(c, torch, a.n, a.k, a.m, a.copies, a.reps)
+        elif a.what == "qmm":
+            r = qmm(c, torch, a.m, a.n, a.k, a.copies, a.reps)
         elif a.what == "gemm":
             r = gemm(c, torch, a.m, a.n, a.k, a.reps, a.copies)
         elif a.what == "attn":

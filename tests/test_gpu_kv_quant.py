@@ -141,11 +141,13 @@ def test_quantized_pages_match_oracle(ctx, name, kv_bits, gs):
     prompt = rng.integers(0, d["vocab"], 45)
     table = rng.permutation(64)[:8].astype(np.int32)
     cache = om.new_cache(128)
-    # chunk A on the GPU, then chunk B on both over the GPU's chunk-A pages
-    m.forward(pool, [dict(tokens=prompt[:29], start_pos=0, block_table=table)])
-    _sync_cache(pool, table, 29, cache, d, kv_bits, gs)
-    got = m.forward(pool, [dict(tokens=prompt[29:], start_pos=29, block_table=table)], nmx.OUT_LOGITS_ALL)
-    ref = om.forward(cache, prompt[29:], 29, all_logits=True)
+    # chunk A on the GPU, then a 4-token chunk B on both over the GPU's
+    # chunk-A pages (the prefill kernel over quantized pages; only chunk B's
+    # own rows are quantized independently on each side)
+    m.forward(pool, [dict(tokens=prompt[:41], start_pos=0, block_table=table)])
+    _sync_cache(pool, table, 41, cache, d, kv_bits, gs)
+    got = m.forward(pool, [dict(tokens=prompt[41:], start_pos=41, block_table=table)], nmx.OUT_LOGITS_ALL)
+    ref = om.forward(cache, prompt[41:], 41, all_logits=True)
     err = check_logits(got, ref)
     pos = len(prompt)
     for _ in range(5):  # teacher-forced decode steps: the fused append quantizes the new token
@@ -214,3 +216,26 @@ def test_quantized_pool_rejects_bad_formats(ctx):
         with pytest.raises(nmx.NmxError) as e:
             nmx.KVPool(m, 8, kv_bits=bits, kv_group_size=gs)
         assert e.value.status == nmx.NMX_ERR_UNSUPPORTED
+
+
+def test_pool_destroyed_and_recreated_between_decodes(ctx):
+    """A decode graph captured over a pool is dropped with the pool: a new
+    pool (which may get the old one's host address) decodes over its own
+    pages, equal to a pool created while it is alive."""
+    from novamlx_b200 import nmx
+    m, _, d = _build(ctx, "qwen", 4, 64)
+    prompt = np.random.default_rng(8).integers(0, d["vocab"], 20)
+    table = np.arange(4, dtype=np.int32)
+
+    def run(pool):
+        first = m.forward(pool, [dict(tokens=prompt, start_pos=0, block_table=table)])
+        return m.decode_greedy(pool, first, [20], table[None], 6)
+
+    p1 = nmx.KVPool(m, 8)
+    run(p1)
+    p1.close()
+    p2 = nmx.KVPool(m, 8, kv_bits=4)
+    ids2 = run(p2)
+    p3 = nmx.KVPool(m, 8, kv_bits=4)
+    ids3 = run(p3)
+    assert np.array_equal(ids2, ids3)
