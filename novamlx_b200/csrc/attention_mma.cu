@@ -7,7 +7,11 @@
 // (16 B chunk c of row r at chunk c ^ (r & 7): conflict-free ldmatrix), and
 // per block runs S = Q·Kᵀ (mma.sync m16n8k16, f16 in, f32 out), an online
 // softmax in the log2 domain on the accumulator fragments, and O += P·V with
-// P taken straight from the S fragments and V fed by ldmatrix.trans. The
+// P taken straight from the S fragments and V fed by ldmatrix.trans. Over
+// quantized pages (4/8-bit codes, group scales and biases) the ring holds the
+// raw page records and each lane dequantizes its own code words straight
+// into its K and V MMA registers (no f16 tile in between). Only rows 0-7 of
+// the MMA tile carry q heads, so only their accumulators are kept. The
 // warps' states merge through shared memory. The splits of one (row, kv
 // head) run as one thread-block cluster (<= 16 CTAs): each CTA stores its
 // (max, denominator) pairs into every CTA of the cluster and each of its
@@ -38,11 +42,6 @@ constexpr int kAStages = 2;   // cp.async stages per warp
 constexpr int kMaxRepA = 8;   // q heads per kv head
 constexpr int kMaxClusterA = kMaxDecodeSplits;  // key splits per (row, kv head): one cluster
 
-__device__ __forceinline__ unsigned cluster_rank() {
-  unsigned r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
 // the two halves of a cluster barrier: arrive (relaxed: the start of the
 // kernel, to mark that this CTA runs; release: after the remote stores) and
 // wait (acquire)
@@ -63,18 +62,131 @@ __device__ __forceinline__ void st_dsmem(void* p, unsigned rank, float v) {
 }
 
 // KQ = 0: f16 pages. KQ = 4 / 8: quantized pages (kv_page_bytes): each warp
-// copies a block's K and V page records into its ring, dequantizes them into
-// its own swizzled f16 tiles right before use, and the MMA path is the same.
+// copies a block's K and V page records into its ring and dequantizes the
+// codes straight into the MMA fragments (w = s·q + b rounded to f16, as a
+// dequantized page holds them), see kfrag_q / vfrag_q.
 template <int D, int KQ>
 struct DecodeSmem {
   static constexpr int TILE = 16 * D * 2;
   static constexpr int PQ = KQ ? kv_page_bytes(D, KQ, 32) : TILE;  // the largest record (group 32)
-  static constexpr int WARP = KQ ? kAStages * 2 * PQ + 2 * TILE : kAStages * 2 * TILE;
-  static constexpr size_t BYTES = TILE + size_t(kAW) * WARP;
+  static constexpr int WARP = KQ ? kAStages * 2 * PQ : kAStages * 2 * TILE;
+  // the warps' merge reuses the rings: [kAW][kMaxRepA][D] + [kMaxRepA][D] floats
+  static constexpr int MERGE = (kAW + 1) * kMaxRepA * D * 4;
+  static constexpr size_t BYTES = TILE + size_t(kAW * WARP > MERGE ? kAW * WARP : MERGE);
 };
 
+// ---- quantized pages: codes to MMA fragments -----------------------------
+// S = Q·Kᵀ (m16n8k16, B = Kᵀ: k = head dim, n = token). The head dim is
+// permuted inside each lane's span so that a lane's B registers come from
+// whole code words: lane (g, t) of n-tile j supplies token 8j + g, dims
+// t·D/4 .. t·D/4 + D/4 - 1 (one quantization group), and k32 step c the
+// dims d0 + δ with d0 = t·D/4 + 8c. The q fragments follow the same order:
+// block 2c + e, register a0 holds dims d0 + qd(e, 0), d0 + qd(e, 1) and a2
+// holds d0 + qd(e, 2), d0 + qd(e, 3).
+template <int KQ>
+__device__ __forceinline__ int qd(int e, int i) {
+  // 4-bit: a word's nibbles pair as (δ, δ + 4); 8-bit: bytes pair as (δ, δ + 1)
+  if constexpr (KQ == 4) return 2 * e + (i >> 1) + 4 * (i & 1);
+  else return 4 * e + i;
+}
+// (v0, v1) f16 bits from two exact f16 codes-plus-1024 x (1024 + q) and the
+// page's scale and bias: w = (x - 1024)·s + b, one rounding
+__device__ __forceinline__ uint32_t dq_pair(uint32_t x, __half2 s2, __half2 b2) {
+  const __half2 k1024 = __float2half2_rn(1024.f);
+  __half2 h = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&x), k1024), s2, b2);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t nib_pair(uint32_t w, int sh) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(r) : "r"(w >> sh), "r"(0x000F000Fu), "r"(0x64006400u));
+  return r;
+}
+__device__ __forceinline__ uint32_t byte_pair(uint32_t w, uint32_t sel) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(r) : "r"(__byte_perm(w, 0u, sel)), "r"(0x00FF00FFu), "r"(0x64006400u));
+  return r;
+}
+// The lane's K code words of one token row (its D/4 dims).
+template <int D, int KQ>
+__device__ __forceinline__ void k_words(const unsigned char* row, int t, uint32_t* wd) {
+  constexpr int NW = D / 4 * KQ / 32;  // 4-bit: D/32, 8-bit: D/16 words
+  const unsigned char* p = row + t * (NW * 4);
+  if constexpr (NW == 2) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    wd[0] = v.x; wd[1] = v.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < NW; i += 4) {
+      const uint4 v = *reinterpret_cast<const uint4*>(p + 4 * i);
+      wd[i] = v.x; wd[i + 1] = v.y; wd[i + 2] = v.z; wd[i + 3] = v.w;
+    }
+  }
+}
+// B registers of k16 blocks 2c (b[0], b[1]) and 2c + 1 (b[2], b[3]) from the
+// lane's words of one token
+template <int KQ>
+__device__ __forceinline__ void kfrag_q(const uint32_t* wd, int c, __half2 s2, __half2 b2, uint32_t* b) {
+  if constexpr (KQ == 4) {
+    const uint32_t w = wd[c];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) b[i] = dq_pair(nib_pair(w, 4 * i), s2, b2);  // (δi, δi+4)
+  } else {
+    const uint32_t w0 = wd[2 * c], w1 = wd[2 * c + 1];
+    b[0] = dq_pair(byte_pair(w0, 0x5140), s2, b2);  // δ0, δ1
+    b[1] = dq_pair(byte_pair(w0, 0x7362), s2, b2);  // δ2, δ3
+    b[2] = dq_pair(byte_pair(w1, 0x5140), s2, b2);  // δ4, δ5
+    b[3] = dq_pair(byte_pair(w1, 0x7362), s2, b2);  // δ6, δ7
+  }
+}
+// O += P·V (B = V: k = token, n = head dim). Lane g's n columns are the dims
+// g·D/8 .. g·D/8 + D/8 - 1 (n-tile j: dim g·D/8 + j), so the accumulator
+// o[j][e] of lane (g, t) is dim (2t + e)·D/8 + j. The lane's B registers for
+// tokens (A, A + 1) come from the two rows' words of its span: the rows'
+// bytes are interleaved first so each register pairs token A with A + 1.
+template <int D, int KQ>
+__device__ __forceinline__ void vfrag_q(const unsigned char* rowA, const unsigned char* rowB, int g, __half2 s2,
+                                        __half2 b2, uint32_t* b) {
+  constexpr int NW = D / 8 * KQ / 32;  // words of the lane's span: 4-bit D/64, 8-bit D/32
+  const unsigned char* pa = rowA + g * (NW * 4);
+  const unsigned char* pb = rowB + g * (NW * 4);
+  uint32_t wa[NW], wb[NW];
+  if constexpr (NW == 1) {
+    wa[0] = *reinterpret_cast<const uint32_t*>(pa);
+    wb[0] = *reinterpret_cast<const uint32_t*>(pb);
+  } else if constexpr (NW == 2) {
+    const uint2 va = *reinterpret_cast<const uint2*>(pa), vb = *reinterpret_cast<const uint2*>(pb);
+    wa[0] = va.x; wa[1] = va.y; wb[0] = vb.x; wb[1] = vb.y;
+  } else {
+    const uint4 va = *reinterpret_cast<const uint4*>(pa), vb = *reinterpret_cast<const uint4*>(pb);
+    wa[0] = va.x; wa[1] = va.y; wa[2] = va.z; wa[3] = va.w;
+    wb[0] = vb.x; wb[1] = vb.y; wb[2] = vb.z; wb[3] = vb.w;
+  }
+#pragma unroll
+  for (int k = 0; k < NW; ++k) {
+    if constexpr (KQ == 4) {
+      // bytes (A0, A1, B0, B1) and (A2, A3, B2, B3): nibble i of each half
+      const uint32_t lo = __byte_perm(wa[k], wb[k], 0x5410), hi = __byte_perm(wa[k], wb[k], 0x7632);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        b[8 * k + i] = dq_pair(nib_pair(lo, 4 * i), s2, b2);
+        b[8 * k + 4 + i] = dq_pair(nib_pair(hi, 4 * i), s2, b2);
+      }
+    } else {
+      // byte i of A and of B, each in the low byte of a half
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint32_t x;
+        asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n"
+            : "=r"(x)
+            : "r"(__byte_perm(wa[k], wb[k], ((4 + i) << 8) | i)), "r"(0x00FF00FFu), "r"(0x64006400u));
+        b[4 * k + i] = dq_pair(x, s2, b2);
+      }
+    }
+  }
+}
+
 template <int D, bool FUSED, int KQ>
-__global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(kAW * 32, KQ ? 4 : 1) paged_decode_mma_kernel(AttnArgs a) {
   constexpr int BT = 16;
   constexpr int CH = D / 8;          // 16-byte chunks per row
   constexpr int TILE = BT * D * 2;   // bytes of one K (or V) block tile
@@ -122,9 +234,6 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
     bt = a.block_tables + long(seq) * a.max_blocks;
   };
   unsigned char* ring = ring_all + warp * SM::WARP;
-  // quantized pages: this warp's dequantized f16 K and V tiles
-  unsigned char* kdq = ring + kAStages * 2 * SM::PQ;
-  unsigned char* vdq = kdq + TILE;
   auto issue = [&](int stage, int b) {
     if (b < b1) {
       if constexpr (KQ == 0) {
@@ -242,20 +351,31 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
   }
   __syncthreads();
 
-  // q fragments (rows 8-15 are zero: a1 = a3 = 0)
+  // q fragments (rows 8-15 are zero: a1 = a3 = 0); quantized pages: in the
+  // permuted head-dim order of kfrag_q
   uint32_t qa[KSTEPS][2];
+  if constexpr (KQ == 0) {
 #pragma unroll
-  for (int kk = 0; kk < KSTEPS; ++kk) {
-    const int r = lane & 7, c = 2 * kk + ((lane >> 3) & 1);
-    ldsm_x2(qa[kk], q_sm + swz<D>(r, c));
+    for (int kk = 0; kk < KSTEPS; ++kk) {
+      const int r = lane & 7, c = 2 * kk + ((lane >> 3) & 1);
+      ldsm_x2(qa[kk], q_sm + swz<D>(r, c));
+    }
+  } else {
+#pragma unroll
+    for (int kk = 0; kk < KSTEPS; ++kk) {
+      const int c = kk >> 1, e = kk & 1, d0 = t * (D / 4) + 8 * c;
+      const half* qc = reinterpret_cast<const half*>(q_sm + swz<D>(g, d0 / 8));  // dims d0 .. d0 + 7
+      qa[kk][0] = pack_half2(__half2float(qc[qd<KQ>(e, 0)]), __half2float(qc[qd<KQ>(e, 1)]));
+      qa[kk][1] = pack_half2(__half2float(qc[qd<KQ>(e, 2)]), __half2float(qc[qd<KQ>(e, 3)]));
+    }
   }
 
   const float sl2 = a.scale * kLog2e;
   // keys up to `last` come from the pages (FUSED: the new token is added apart)
   const int last = FUSED ? pos - 1 : pos;
-  float o[NT][4];
+  float o[NT][2];  // rows 0-7 of the MMA tile (rows 8-15 are the zero padding)
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+  for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = 0.f;
   float m_r = -INFINITY, l_r = 0.f;
 
   int stage = 0;
@@ -264,22 +384,48 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
     __syncwarp();
     const unsigned char* kt = ring + stage * 2 * TILE;
     const unsigned char* vt = kt + TILE;
-    if constexpr (KQ != 0) {
-      const unsigned char* kraw = ring + stage * 2 * SM::PQ;
-      dequant_page_warp<D>(kraw, KQ, a.kv_gs, kdq);
-      dequant_page_warp<D>(kraw + SM::PQ, KQ, a.kv_gs, vdq);
-      __syncwarp();
-      kt = kdq;
-      vt = vdq;
-    }
-    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    float s[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    // quantized pages: V's B registers (tokens 2t, 2t + 1 | 2t + 8, 2t + 9)
+    uint32_t vb[2][KQ ? NT : 1];
+    if constexpr (KQ == 0) {
 #pragma unroll
-    for (int kk = 0; kk < KSTEPS; ++kk) {
-      uint32_t r[4];
-      const int rr = (lane & 7) + ((lane >> 4) << 3), cc = 2 * kk + ((lane >> 3) & 1);
-      ldsm_x4(r, kt + swz<D>(rr, cc));
-      mma_f16(s[0], qa[kk][0], 0u, qa[kk][1], 0u, r[0], r[1]);
-      mma_f16(s[1], qa[kk][0], 0u, qa[kk][1], 0u, r[2], r[3]);
+      for (int kk = 0; kk < KSTEPS; ++kk) {
+        uint32_t r[4];
+        const int rr = (lane & 7) + ((lane >> 4) << 3), cc = 2 * kk + ((lane >> 3) & 1);
+        ldsm_x4(r, kt + swz<D>(rr, cc));
+        mma_f16_top(s[0], qa[kk][0], qa[kk][1], r[0], r[1]);
+        mma_f16_top(s[1], qa[kk][0], qa[kk][1], r[2], r[3]);
+      }
+    } else {
+      // page record: codes [16][R], scales [16][ng], biases [16][ng]
+      constexpr int R = D * KQ / 8;
+      const unsigned char* kraw = ring + stage * 2 * SM::PQ;
+      const unsigned char* vraw = kraw + SM::PQ;
+      const int ng = D / a.kv_gs;
+      const half* ksc = reinterpret_cast<const half*>(kraw + 16 * R);
+      const half* vsc = reinterpret_cast<const half*>(vraw + 16 * R);
+      const int kgrp = t * (D / 4) / a.kv_gs, vgrp = g * (D / 8) / a.kv_gs;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int tok = 8 * j + g;
+        uint32_t wd[D / 4 * KQ / 32];
+        k_words<D, KQ>(kraw + tok * R, t, wd);
+        const __half2 s2 = __half2half2(ksc[tok * ng + kgrp]), b2 = __half2half2(ksc[16 * ng + tok * ng + kgrp]);
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t bq[4];
+          kfrag_q<KQ>(wd, c, s2, b2, bq);
+          mma_f16_top(s[j], qa[2 * c][0], qa[2 * c][1], bq[0], bq[1]);
+          mma_f16_top(s[j], qa[2 * c + 1][0], qa[2 * c + 1][1], bq[2], bq[3]);
+        }
+      }
+#pragma unroll
+      for (int tp = 0; tp < 2; ++tp) {
+        const int A = 2 * t + 8 * tp;
+        const __half2 s2 = __halves2half2(vsc[A * ng + vgrp], vsc[(A + 1) * ng + vgrp]);
+        const __half2 b2 = __halves2half2(vsc[16 * ng + A * ng + vgrp], vsc[16 * ng + (A + 1) * ng + vgrp]);
+        vfrag_q<D, KQ>(vraw + A * R, vraw + (A + 1) * R, g, s2, b2, vb[tp]);
+      }
     }
     // scale to log2 units, mask keys past `last`, online softmax of row g
     const int tb = b * BT;
@@ -309,13 +455,18 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
       o[nt][1] *= corr;
     }
     const uint32_t pa0 = pack_half2(p[0], p[1]), pa2 = pack_half2(p[2], p[3]);
+    if constexpr (KQ == 0) {
 #pragma unroll
-    for (int np = 0; np < NT / 2; ++np) {
-      uint32_t r[4];
-      const int rr = (lane & 7) + (((lane >> 3) & 1) << 3), cc = 2 * np + (lane >> 4);
-      ldsm_x4_t(r, vt + swz<D>(rr, cc));
-      mma_f16(o[2 * np], pa0, 0u, pa2, 0u, r[0], r[1]);
-      mma_f16(o[2 * np + 1], pa0, 0u, pa2, 0u, r[2], r[3]);
+      for (int np = 0; np < NT / 2; ++np) {
+        uint32_t r[4];
+        const int rr = (lane & 7) + (((lane >> 3) & 1) << 3), cc = 2 * np + (lane >> 4);
+        ldsm_x4_t(r, vt + swz<D>(rr, cc));
+        mma_f16_top(o[2 * np], pa0, pa2, r[0], r[1]);
+        mma_f16_top(o[2 * np + 1], pa0, pa2, r[2], r[3]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < NT; ++j) mma_f16_top(o[j], pa0, pa2, vb[0][j], vb[1][j]);
     }
     __syncwarp();
     issue(stage, b + 2 * kAW);
@@ -336,7 +487,13 @@ __global__ void __launch_bounds__(kAW * 32) paged_decode_mma_kernel(AttnArgs a) 
     }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      *reinterpret_cast<float2*>(s_o + (warp * kMaxRepA + g) * D + nt * 8 + 2 * t) = make_float2(o[nt][0], o[nt][1]);
+      if constexpr (KQ == 0) {
+        *reinterpret_cast<float2*>(s_o + (warp * kMaxRepA + g) * D + nt * 8 + 2 * t) = make_float2(o[nt][0], o[nt][1]);
+      } else {
+        // n-tile nt, column 2t + e: dim (2t + e)·D/8 + nt
+        s_o[(warp * kMaxRepA + g) * D + (2 * t) * (D / 8) + nt] = o[nt][0];
+        s_o[(warp * kMaxRepA + g) * D + (2 * t + 1) * (D / 8) + nt] = o[nt][1];
+      }
     }
   }
   {

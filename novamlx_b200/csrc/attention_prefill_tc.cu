@@ -140,11 +140,11 @@ __global__ void __launch_bounds__(kPTThreads, 1) paged_prefill_tc_kernel(const _
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_free[s], kPTRows);
+      mbar_init(&s_free[s], kPTRows / 32);  // one arrival per softmax warp
     }
-    mbar_init(&p_full, kPTRows);
+    mbar_init(&p_full, kPTRows / 32);
     mbar_init(&o_done, 1);
-    mbar_init(&q_ready, kPTRows);
+    mbar_init(&q_ready, kPTRows / 32);
     s_fail = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -256,7 +256,7 @@ __global__ void __launch_bounds__(kPTThreads, 1) paged_prefill_tc_kernel(const _
       for (int c = 0; c < D / 64; ++c) tmem_st32(lane_base + L::kColQ + 32 * c, qw + 32 * c);
       tmem_st_wait();
       tc::tc_fence_before();
-      mbar_arrive(&q_ready);
+      tc::warp_arrive(&q_ready);
     }
     // tcgen05.ld / st are warp-collective: every branch around them below
     // is uniform over the warp (waits are agreed with __all_sync, the O
@@ -324,7 +324,7 @@ __global__ void __launch_bounds__(kPTThreads, 1) paged_prefill_tc_kernel(const _
         }
       }
       tc::tc_fence_before();
-      mbar_arrive(&s_free[sb]);
+      tc::warp_arrive(&s_free[sb]);
       // P's columns are free once the previous P·V has completed
       if (j > 0 && !waited) {
         ok = __all_sync(0xffffffffu, mbar_wait(&o_done, (j - 1) & 1, lim));
@@ -335,7 +335,7 @@ __global__ void __launch_bounds__(kPTThreads, 1) paged_prefill_tc_kernel(const _
       tmem_st32(lane_base + L::kColP + 32, pw + 32);
       tmem_st_wait();
       tc::tc_fence_before();
-      mbar_arrive(&p_full);
+      tc::warp_arrive(&p_full);
     }
     // ------------------------------------------------------------ epilogue
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&o_done, (nchunks - 1) & 1, lim));

@@ -44,6 +44,20 @@ __device__ __forceinline__ void mma_f16(float* d, uint32_t a0, uint32_t a1, uint
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// The same MMA when rows 8-15 of A are zero (a1 = a3 = 0): only the
+// accumulators of rows 0-7 (d[0], d[1]) are kept; rows 8-15 read zeros and
+// their results are dropped, so they hold no registers across calls.
+__device__ __forceinline__ void mma_f16_top(float* d, uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  float x2, x3;
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%11,%12,%13};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(x2), "=f"(x3)
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1), "f"(d[0]), "f"(d[1]), "f"(0.f), "f"(0.f));
+  (void)x2;
+  (void)x3;
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
@@ -163,10 +177,6 @@ __device__ __forceinline__ void dequant_page(const unsigned char* rec, int bits,
                               : dq8_chunk(*reinterpret_cast<const uint2*>(rec + r * rowbytes + 8 * c), s2, b2);
     *reinterpret_cast<uint4*>(tile + swz<D>(r, c)) = o;
   }
-}
-template <int D>
-__device__ __forceinline__ void dequant_page_warp(const unsigned char* rec, int bits, int gs, unsigned char* tile) {
-  dequant_page<D>(rec, bits, gs, tile, threadIdx.x & 31, 32);
 }
 
 }  // namespace

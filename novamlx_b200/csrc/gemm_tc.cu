@@ -99,13 +99,13 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
 
   if (tid == 0) {
     for (int s = 0; s < kTS; ++s) {
-      mbar_init(&full[s], 1 + kDW * 32);  // TMA thread (expect_tx) + the dequant threads
+      mbar_init(&full[s], 1 + kDW);  // TMA thread (expect_tx) + one arrival per dequant warp
       mbar_init(&empty[s], 1);       // tcgen05.commit
     }
     mbar_init(&acc_bar, 1);
     for (int s = 0; s < kRS; ++s) {
       mbar_init(&raw_full[s], 1);      // record loader (expect_tx)
-      mbar_init(&raw_empty[s], kDW * 32);  // the dequant threads, after the block's second stage
+      mbar_init(&raw_empty[s], kDW);  // the dequant warps, after the block's second stage
     }
     s_fail = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -192,14 +192,12 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
     // ----------------------------------------- dequant warps: weight tile rows
     for (int kt = 0; kt < KT; ++kt) {
       const int s = kt % kTS;
-      if (kt >= kTS && !mbar_wait(&empty[s], ((kt / kTS) - 1) & 1, lim)) {
-        atomicOr(a.err, kErrPipeWait);
-        s_fail = 1;
-        break;
-      }
       unsigned char* B = smem + s * kStageBytes + kABytes;
       const int blk = kt >> 1, gi = kt & 1, rs = blk % kRS;
-      if (gi == 0 && !mbar_wait(&raw_full[rs], (blk / kRS) & 1, lim)) {
+      // waits agreed over the warp: its lanes arrive together (warp_arrive)
+      bool ok = kt < kTS || mbar_wait(&empty[s], ((kt / kTS) - 1) & 1, lim);
+      ok = ok && (gi != 0 || mbar_wait(&raw_full[rs], (blk / kRS) & 1, lim));
+      if (!__all_sync(0xffffffffu, ok)) {
         atomicOr(a.err, kErrPipeWait);
         s_fail = 1;
         break;
@@ -230,8 +228,8 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
       }
       // generic-proxy writes, read by the tensor core's async proxy
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_arrive(&full[s]);
-      if (gi == 1) mbar_arrive(&raw_empty[rs]);  // the block's records are read
+      tc::warp_arrive(&full[s]);
+      if (gi == 1) tc::warp_arrive(&raw_empty[rs]);  // the block's records are read
     }
 
     // ------------------------------------------------------------ epilogue

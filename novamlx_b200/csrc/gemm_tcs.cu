@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
 
   if (tid == 0) {
     for (int s = 0; s < kAST; ++s) {
-      mbar_init(&a_full[s], 128);  // one dequant warpgroup per unit
+      mbar_init(&a_full[s], 4);  // the four warps of one dequant warpgroup per unit
       mbar_init(&a_empty[s], 1);
     }
     for (int s = 0; s < kXSMax; ++s) {
@@ -269,7 +269,7 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
     }
     for (int s = 0; s < kRSMax; ++s) {
       mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_empty[s], 128);
+      mbar_init(&raw_empty[s], 4);
     }
     mbar_init(&acc_bar, 1);
     s_fail = 0;
@@ -393,12 +393,10 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
     const int as = dg;
     int rs = dg % a.rs, rph = (dg / a.rs) & 1;
     for (int i = dg; i < units; i += kDG) {
-      if (i >= kAST && !mbar_wait(&a_empty[as], ((i / kAST) - 1) & 1, lim)) {
-        atomicOr(a.err, kErrPipeWait);
-        s_fail = 1;
-        break;
-      }
-      if (!mbar_wait(&raw_full[rs], rph, lim)) {
+      // waits agreed over the warp: its lanes arrive together (warp_arrive)
+      bool ok = i < kAST || mbar_wait(&a_empty[as], ((i / kAST) - 1) & 1, lim);
+      ok = ok && mbar_wait(&raw_full[rs], rph, lim);
+      if (!__all_sync(0xffffffffu, ok)) {
         atomicOr(a.err, kErrPipeWait);
         s_fail = 1;
         break;
@@ -418,14 +416,14 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
       }
       uint32_t out[2][32];
       dequant_row_words(c, s2, s16, b2, out);
-      mbar_arrive(&raw_empty[rs]);  // the slot's bytes are in registers
+      tc::warp_arrive(&raw_empty[rs]);  // the slot's bytes are in registers
       tc::tc_fence_after();         // after the wait for the stage's last MMAs
       const uint32_t acol = lane_base + uint32_t(kAccCols + as * kAStageCols);
       tmem_st32(acol, out[0]);
       tmem_st32(acol + 32, out[1]);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc::tc_fence_before();
-      mbar_arrive(&a_full[as]);
+      tc::warp_arrive(&a_full[as]);
       rs += kDG;
       while (rs >= a.rs) {
         rs -= a.rs;

@@ -23,6 +23,14 @@ __device__ __forceinline__ void mbar_init(uint64_t* b, unsigned count) {
 __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sa_(b)) : "memory");
 }
+// One arrival for the whole warp (the barrier counts warps): the lanes'
+// prior writes are ordered before lane 0's release-arrive by __syncwarp.
+// An arrive is a shared-memory atomic, so per-thread arrivals on a hot
+// barrier serialise hundreds of atomics per handoff.
+__device__ __forceinline__ void warp_arrive(uint64_t* b) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(b);
+}
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* b, unsigned bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sa_(b)), "r"(bytes) : "memory");
 }

@@ -148,12 +148,14 @@ def test_qmatmul_records_tensor_core_gemm(env, M, N, K):
 
 @pytest.mark.parametrize("M,N,K", [(9, 4096, 4096), (16, 1024, 512), (33, 6144, 1024), (64, 4096, 4096),
                                    (80, 16384, 1024), (128, 1024, 2048), (100, 512, 14336), (21, 6144, 4096),
-                                   (21, 4096, 14336), (32, 55296, 5120), (112, 4096, 4096)])
+                                   (21, 4096, 14336), (32, 55296, 5120), (112, 4096, 4096), (21, 896, 5120),
+                                   (40, 384, 1024), (17, 128, 4096), (64, 1280, 27648), (65, 1792, 5120)])
 def test_qmatmul_records_decode_batch_gemm(env, M, N, K):
     """9..112 rows go through the decode-batch tcgen05 GEMM (weights as the
     MMA's rows, rows of x as its columns, K split over the SMs with a
-    deterministic last-arriver sum; 113..128 rows through the prefill GEMM):
-    equals the oracle in one launch, and repeated calls agree bit for bit."""
+    deterministic last-arriver sum; 113..128 rows through the prefill GEMM),
+    odd tile counts and a single tile included: equals the oracle in one
+    launch, and repeated calls agree bit for bit."""
     torch, nmx, ctx = env
     rng = np.random.default_rng(7 * M + N + K)
     w = rng.standard_normal((N, K), dtype=np.float32) * 0.02
