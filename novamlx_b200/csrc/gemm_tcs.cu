@@ -57,8 +57,9 @@ using tc::smem_desc;
 
 constexpr int kDG = 4;                      // dequant warpgroups (they take units in turn)
 constexpr int kSDW = 4 * kDG;               // dequant / epilogue warps
-constexpr int kSThreads = (kSDW + 3) * 32;  // + MMA, x-tile and record-loader warps
-constexpr int kSWMma = kSDW, kSWTma = kSDW + 1, kSWRec = kSDW + 2;
+constexpr int kNIMax = 4;                   // MMA-issuing warps (one per dequant warpgroup at most)
+constexpr int kSThreads = (kSDW + kNIMax + 2) * 32;  // + MMA-issue, x-tile and record-loader warps
+constexpr int kSWMma = kSDW, kSWTma = kSDW + kNIMax, kSWRec = kSDW + kNIMax + 1;
 constexpr int kAST = 4;                     // dequantized weight stages, in TMEM
 constexpr int kAStageCols = 64;             // 128 k of f16, two per 32-bit column
 constexpr int kAccCols = 512 - kAST * kAStageCols;  // accumulator columns
@@ -75,6 +76,7 @@ struct TcsArgs {
   int M, NT, K, nb;        // rows of x, MMA N, K, K / 128
   int n_atiles;            // weight tiles (SiLU: 2 per output tile)
   int tg, S;               // tiles per group, K shares
+  int ni;                  // MMA-issuing warps (divides 4 and tg)
   int rs, xs;              // raw slots, x stages
   uint32_t idesc;
   long long pair_tiles;    // SiLU: 16-row tile offset of the up rows
@@ -253,6 +255,9 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
   const int b0 = int((long long)share * a.nb / a.S), b1 = int((long long)(share + 1) * a.nb / a.S);
   const int nblk = b1 - b0;
   const int units = nblk * ntl;  // (block, tile) pairs, block-major
+  // issuers: the largest of a.ni, a.ni / 2, .. dividing this CTA's tile count
+  int ni = a.ni;
+  while (ntl % ni) ni >>= 1;
   const int NT = a.NT;
   const int xhalf = NT * 128;    // bytes of one 64-k half of an x stage
   unsigned char* stX = smem;
@@ -265,13 +270,13 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
     }
     for (int s = 0; s < kXSMax; ++s) {
       mbar_init(&x_full[s], 1);
-      mbar_init(&x_empty[s], 1);
+      mbar_init(&x_empty[s], ni);  // each issuer, after its last tile of the block
     }
     for (int s = 0; s < kRSMax; ++s) {
       mbar_init(&raw_full[s], 1);
       mbar_init(&raw_empty[s], 4);
     }
-    mbar_init(&acc_bar, 1);
+    mbar_init(&acc_bar, ni);
     s_fail = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -336,18 +341,24 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
         }
       }
     }
-  } else if (warp == kSWMma) {
+  } else if (warp >= kSWMma && warp < kSWMma + kNIMax) {
     // ------------------------------------------------------------ MMA issue
-    if (lane == 0) {
-      // one thread issues every MMA: keep its per-MMA work to a few adds
-      // (descriptor start addresses advance in 16-byte units)
+    // Issuer j (lane 0 of warp kSWMma + j) takes the units i ≡ j (mod ni):
+    // the tiles ti ≡ j and the A stages i mod 4 ≡ j (mod ni), so every
+    // accumulator and every A stage has one issuer. An issuing thread pays
+    // tens of cycles per tcgen05.mma, so one thread alone caps the tensor
+    // pipe; ni threads keep up to ni instruction streams in flight.
+    const int j = warp - kSWMma;
+    if (lane == 0 && j < ni) {
+      // per-MMA work is a few adds (descriptor start addresses advance in
+      // 16-byte units)
       const uint64_t xdesc0 = smem_desc(stX);
       const uint32_t xstage_d = uint32_t(2 * xhalf) >> 4, xhalf_d = uint32_t(xhalf) >> 4;
       const uint32_t a0 = taddr + uint32_t(kAccCols), idesc = a.idesc;
-      int ti = 0, as = 0, aph = 0, xs = 0, xph = 0;
+      int ti = j, as = j, aph = 0, xs = 0, xph = 0;
       uint32_t first = 0u;  // 0 until the first block is in the accumulators
-      for (int i = 0; i < units; ++i) {
-        bool ok = !(ti == 0 && !mbar_wait(&x_full[xs], xph, lim));
+      for (int i = j; i < units; i += ni) {
+        bool ok = !(ti == j && !mbar_wait(&x_full[xs], xph, lim));
         if (ok && !mbar_wait(&a_full[as], aph, lim)) ok = false;
         if (!ok) {
           atomicOr(a.err, kErrPipeWait);
@@ -363,13 +374,15 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
           mma_f16_ta(d, A + 8 * k16, bd + uint64_t((k16 >> 2) * xhalf_d + 2 * (k16 & 3)), idesc,
                      k16 ? 1u : first);
         tc::mma_commit(&a_empty[as]);
-        if (++as == kAST) {
-          as = 0;
+        as += ni;
+        if (as >= kAST) {
+          as -= kAST;
           aph ^= 1;
         }
-        if (++ti == ntl) {
+        ti += ni;
+        if (ti >= ntl) {
           tc::mma_commit(&x_empty[xs]);
-          ti = 0;
+          ti -= ntl;
           first = 1u;
           if (++xs == a.xs) {
             xs = 0;
@@ -379,7 +392,7 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
       }
       tc::mma_commit(&acc_bar);
     }
-  } else {
+  } else if (warp < kSDW) {
     // ------------------------------------------------ dequantize the tiles
     // warpgroup dg takes units dg, dg + kDG, ...; thread: TMEM lane L (the
     // warp's lane quarter), both groups of weight row lane_row(L)
@@ -583,13 +596,15 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
 }
 
 struct TcsPlan {
-  int NT = 0, tg = 0, groups = 0, S = 0, rs = 0, xs = 0;
+  int NT = 0, tg = 0, groups = 0, S = 0, rs = 0, xs = 0, ni = 1;
   size_t smem = 0, partial_floats = 0;
 };
 
 // Tiles per group and K shares: the fewest weight units (tile × K block) on
-// the busiest CTA over one wave of SMs, with the x tile's L2 reads and the
-// partial sums' round trip counted against it.
+// the busiest CTA over one wave of SMs, with the x tile's L2 reads, the
+// partial sums' round trip and the MMA issue rate counted against it: one
+// issuing thread needs about twice a unit's streaming time for its eight
+// MMAs, two or four issuers (tile counts divisible by them) do not.
 TcsPlan plan_tcs(int M, int N_out, int K, int epi, int num_sms) {
   TcsPlan p;
   p.NT = (M + 15) / 16 * 16;
@@ -605,14 +620,17 @@ TcsPlan plan_tcs(int M, int N_out, int K, int epi, int num_sms) {
       const long long waves = (ctas + num_sms - 1) / num_sms;
       if (waves > 1 && S > 1) break;
       const int upc = tga * ((nb + S - 1) / S);
+      const int ni = tga % 4 == 0 ? 4 : (tga % 2 == 0 ? 2 : 1);
+      const double issue = std::max(1.0, 1.9 / ni);
       const double x_cost = 0.5 * double(p.NT) * 256.0 / (double(tga) * 8 * kRecG);
       const double p_cost = S > 1 ? 0.5 * double(tga) * p.NT * 128 * 8 / (double(upc) * 8 * kRecG) : 0.0;
-      const double cost = double(waves) * upc * (1.0 + x_cost + p_cost) + 1e-6 * double(ctas);
+      const double cost = double(waves) * upc * (issue + x_cost + p_cost) + 1e-6 * double(ctas);
       if (cost < best) {
         best = cost;
         p.tg = tga;
         p.groups = groups;
         p.S = S;
+        p.ni = ni;
       }
     }
   }
@@ -693,6 +711,7 @@ nmx_status_t qgemm_tcs(Ctx* c, const GemvDLArgs& a, int epi) {
   g.n_atiles = (a.N / 128) * (epi == EPI_SILU ? 2 : 1);
   g.tg = p.tg;
   g.S = p.S;
+  g.ni = p.ni;
   g.rs = p.rs;
   g.xs = p.xs;
   g.idesc = tc::idesc_f16(128, p.NT);
