@@ -407,9 +407,7 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
     int rs = dg % a.rs, rph = (dg / a.rs) & 1;
     for (int i = dg; i < units; i += kDG) {
       // waits agreed over the warp: its lanes arrive together (warp_arrive)
-      bool ok = i < kAST || mbar_wait(&a_empty[as], ((i / kAST) - 1) & 1, lim);
-      ok = ok && mbar_wait(&raw_full[rs], rph, lim);
-      if (!__all_sync(0xffffffffu, ok)) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&raw_full[rs], rph, lim))) {
         atomicOr(a.err, kErrPipeWait);
         s_fail = 1;
         break;
@@ -430,6 +428,13 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
       uint32_t out[2][32];
       dequant_row_words(c, s2, s16, b2, out);
       tc::warp_arrive(&raw_empty[rs]);  // the slot's bytes are in registers
+      // only the TMEM stores wait for the stage's previous MMAs: the loads
+      // and the dequantisation above overlap them
+      if (!__all_sync(0xffffffffu, i < kAST || mbar_wait(&a_empty[as], ((i / kAST) - 1) & 1, lim))) {
+        atomicOr(a.err, kErrPipeWait);
+        s_fail = 1;
+        break;
+      }
       tc::tc_fence_after();         // after the wait for the stage's last MMAs
       const uint32_t acol = lane_base + uint32_t(kAccCols + as * kAStageCols);
       tmem_st32(acol, out[0]);
@@ -621,7 +626,8 @@ TcsPlan plan_tcs(int M, int N_out, int K, int epi, int num_sms) {
       if (waves > 1 && S > 1) break;
       const int upc = tga * ((nb + S - 1) / S);
       const int ni = tga % 4 == 0 ? 4 : (tga % 2 == 0 ? 2 : 1);
-      const double issue = std::max(1.0, 1.9 / ni);
+      // (more issuers also shorten each unit's hand-over: a small preference)
+      const double issue = std::max(1.0, 1.9 / ni) * (1.0 + 0.03 * (4 / ni - 1));
       const double x_cost = 0.5 * double(p.NT) * 256.0 / (double(tga) * 8 * kRecG);
       const double p_cost = S > 1 ? 0.5 * double(tga) * p.NT * 128 * 8 / (double(upc) * 8 * kRecG) : 0.0;
       const double cost = double(waves) * upc * (issue + x_cost + p_cost) + 1e-6 * double(ctas);
