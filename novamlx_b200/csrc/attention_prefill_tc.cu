@@ -11,8 +11,11 @@
 //     copied from a row past the pool's end, which the copy fills with zeros;
 //   * warp 5 (one thread) issues S = Q·Kᵀ (M 128 rows, N 128 keys, K = head
 //     dim; Q from TMEM, K from shared memory, K-major) into one of two TMEM
-//     S buffers, and O += P·V (P from TMEM, V from shared memory read
-//     MN-major, i.e. straight from the page layout) into the TMEM output;
+//     S buffers, and warp 6 (one thread) O += P·V (P from TMEM, V from
+//     shared memory read MN-major, i.e. straight from the page layout) into
+//     the TMEM output: an issuing thread pays tens of cycles per MMA, so
+//     the two streams go from two threads; a K/V stage is free once both
+//     have committed it;
 //   * warps 0-3 (thread i = tile row i = TMEM lane i) read their S row, mask
 //     keys past the row's position, and run the online softmax in the log2
 //     domain with a lazy reference maximum: p = exp2(s - m_ref) and m_ref
@@ -45,8 +48,8 @@ using tc::sa_;
 constexpr int kPTRows = 128;    // tile rows: (position, q head) pairs
 constexpr int kPTKeys = 128;    // keys per chunk (8 pages)
 constexpr int kPTStages = 3;    // K/V chunk stages
-constexpr int kPTWarpTma = 4, kPTWarpMma = 5;
-constexpr int kPTThreads = 6 * 32;
+constexpr int kPTWarpTma = 4, kPTWarpMma = 5, kPTWarpMmaO = 6;  // S = Q·Kᵀ issuer, O += P·V issuer
+constexpr int kPTThreads = 7 * 32;
 constexpr int kBox = 16 * 64 * 2;  // one tensor copy: 16 tokens × 64 d of f16
 
 template <int D>
@@ -136,7 +139,7 @@ __global__ void __launch_bounds__(kPTThreads, 1) paged_prefill_tc_kernel(const _
   if (tid == 0) {
     for (int s = 0; s < kPTStages; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&kv_empty[s], 2);  // the S issuer (K read) and the O issuer (V read)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
@@ -194,7 +197,6 @@ __global__ void __launch_bounds__(kPTThreads, 1) paged_prefill_tc_kernel(const _
     // ------------------------------------------------------------ MMA issue
     if (lane == 0) {
       const uint32_t idS = tc::idesc_f16(128, kPTKeys);
-      const uint32_t idO = tc::idesc_f16(128, D) | (1u << 16);  // B (V) MN-major
       bool ok = mbar_wait(&q_ready, 0, lim);
       auto issue_s = [&](int j) -> bool {
         const int st = j % kPTStages, sb = j & 1;
@@ -209,12 +211,23 @@ __global__ void __launch_bounds__(kPTThreads, 1) paged_prefill_tc_kernel(const _
         tc::mma_commit(&s_full[sb]);
         return true;
       };
-      if (ok) ok = issue_s(0);
+      // one issuing thread pays tens of cycles per tcgen05.mma: the S
+      // products and the P·V products come from two threads (two warps)
       for (int j = 0; ok && j < nchunks; ++j) {
-        if (j + 1 < nchunks && !issue_s(j + 1)) {
-          ok = false;
-          break;
-        }
+        if (!issue_s(j)) ok = false;
+        else tc::mma_commit(&kv_empty[j % kPTStages]);
+      }
+      if (!ok) {
+        atomicOr(a.err, kErrPipeWait);
+        s_fail = 1;
+      }
+    }
+  } else if (warp == kPTWarpMmaO) {
+    if (lane == 0) {
+      const uint32_t idO = tc::idesc_f16(128, D) | (1u << 16);  // B (V) MN-major
+      bool ok = true;
+      for (int j = 0; ok && j < nchunks; ++j) {
+        // P(j) is in TMEM (which also means S(j) and K(j) are done with)
         if (!mbar_wait(&p_full, j & 1, lim)) {
           ok = false;
           break;

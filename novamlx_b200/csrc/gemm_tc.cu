@@ -35,14 +35,20 @@ namespace nmx {
 
 namespace {
 
-constexpr int kTM = 128;          // rows of x per CTA (MMA M)
+constexpr int kTM = 128;          // rows of x per MMA (MMA M); a CTA takes MT such sub-tiles
 constexpr int kTN = 256;          // MMA N: weight rows per CTA
 constexpr int kTK = 64;           // k per stage (one group)
-constexpr int kTS = 3;            // stages
 constexpr int kRS = 3;            // raw record slots (one 128-k block of the 16 tiles each)
-constexpr int kABytes = kTM * kTK * 2;   // 16 KB
+constexpr int kABytes = kTM * kTK * 2;   // 16 KB per x sub-tile
 constexpr int kBBytes = kTN * kTK * 2;   // 32 KB
-constexpr int kStageBytes = kABytes + kBBytes;
+// stage: MT x sub-tiles, then the dequantized weight tile; 3 stages for one
+// sub-tile, 2 for two (the shared-memory budget)
+template <int MT>
+struct TcStages {
+  static constexpr int kTS = MT == 1 ? 3 : 2;
+  static constexpr int kStageBytes = MT * kABytes + kBBytes;
+  static constexpr size_t kSmem = size_t(kTS) * kStageBytes + size_t(kRS) * (16 * tc::kRecPad) + 1024;
+};
 constexpr int kDW = 8;            // dequant / epilogue warps (one weight row per thread)
 constexpr int kGThreads = (kDW + 3) * 32;  // + MMA, x-tile and record-loader warps
 constexpr int kWMma = kDW, kWTma = kDW + 1, kWRec = kDW + 2;
@@ -75,7 +81,7 @@ struct GemmArgs {
   unsigned* err;
 };
 
-template <int EPI>
+template <int EPI, int MT>
 __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                                                  const __grid_constant__ CUtensorMap tmap_w,
                                                                  GemmArgs a) {
@@ -83,6 +89,7 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
   // 1024-byte aligned, derived from the shared array itself so that its
   // loads and stores compile to shared-memory (not generic) accesses
   unsigned char* smem = smem_raw + ((1024u - (tc::sa_(smem_raw) & 1023u)) & 1023u);
+  constexpr int kTS = TcStages<MT>::kTS, kStageBytes = TcStages<MT>::kStageBytes;
   __shared__ __align__(8) uint64_t full[kTS];
   __shared__ __align__(8) uint64_t empty[kTS];
   __shared__ __align__(8) uint64_t acc_bar;
@@ -93,7 +100,7 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const unsigned lim = wait_polls(a.err);  // polls before a pipeline wait gives up
-  const int m0 = blockIdx.x * kTM;
+  const int m0 = blockIdx.x * kTM * MT;
   const int nt = blockIdx.y;  // output tile
   const int KT = a.K / kTK, nb = a.K / 128;
 
@@ -111,7 +118,8 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == kWMma) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sa_(&s_taddr)), "r"(kTN)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sa_(&s_taddr)),
+                 "r"(kTN * MT)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -156,12 +164,14 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
           break;
         }
         unsigned char* dst = smem + s * kStageBytes;
-        mbar_expect_tx(&full[s], kABytes);
-        asm volatile(
-            "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-                "r"(sa_(dst)),
-            "l"(&tmap_x), "r"(kt * kTK), "r"(m0), "r"(sa_(&full[s]))
-            : "memory");
+        mbar_expect_tx(&full[s], MT * kABytes);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+          asm volatile(
+              "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+              "[%4];" ::"r"(sa_(dst + mt * kABytes)),
+              "l"(&tmap_x), "r"(kt * kTK), "r"(m0 + mt * kTM), "r"(sa_(&full[s]))
+              : "memory");
       }
     }
   } else if (warp == kWMma) {
@@ -179,11 +189,14 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
           break;
         }
         tc_fence_after();
-        const uint64_t ad = desc0 + uint64_t(s * kStageD), bd = ad + kAD;
+        const uint64_t ad = desc0 + uint64_t(s * kStageD), bd = ad + MT * kAD;
         const uint32_t first = kt ? 1u : 0u;
+        // the dequantized weight stage serves every x sub-tile
 #pragma unroll
-        for (int k16 = 0; k16 < kTK / 16; ++k16)
-          mma_f16_tc(taddr, ad + 2 * k16, bd + 2 * k16, k16 ? 1u : first);
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int k16 = 0; k16 < kTK / 16; ++k16)
+            mma_f16_tc(taddr + uint32_t(mt * kTN), ad + mt * kAD + 2 * k16, bd + 2 * k16, k16 ? 1u : first);
         mma_commit(&empty[s]);
       }
       mma_commit(&acc_bar);
@@ -192,7 +205,7 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
     // ----------------------------------------- dequant warps: weight tile rows
     for (int kt = 0; kt < KT; ++kt) {
       const int s = kt % kTS;
-      unsigned char* B = smem + s * kStageBytes + kABytes;
+      unsigned char* B = smem + s * kStageBytes + MT * kABytes;
       const int blk = kt >> 1, gi = kt & 1, rs = blk % kRS;
       // waits agreed over the warp: its lanes arrive together (warp_arrive)
       bool ok = kt < kTS || mbar_wait(&empty[s], ((kt / kTS) - 1) & 1, lim);
@@ -240,10 +253,11 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
     tc_fence_after();
     // warp w reads TMEM lanes 32 (w % 4) .. +31 (its rows) and half the columns
     const int quad = warp & 3, chalf = warp >> 2;
-    const int m = m0 + 32 * quad + lane;
-    const uint32_t lane_addr = taddr + (uint32_t(32 * quad) << 16);
     constexpr int OUT = EPI == EPI_SILU ? 128 : kTN;  // output columns of the tile
+    for (int mt = 0; mt < MT; ++mt)
     for (int c0 = chalf * (OUT / 2); c0 < (chalf + 1) * (OUT / 2); c0 += 32) {
+      const int m = m0 + mt * kTM + 32 * quad + lane;
+      const uint32_t lane_addr = taddr + uint32_t(mt * kTN) + (uint32_t(32 * quad) << 16);
       float v[32], u[32];
       tmem_ld32(lane_addr + c0, v);
       if constexpr (EPI == EPI_SILU) tmem_ld32(lane_addr + 128 + c0, u);
@@ -289,23 +303,33 @@ __global__ void __launch_bounds__(kGThreads, 1) qgemm_tc_kernel(const __grid_con
   __syncthreads();
   if (warp == kWMma) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(kTN) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(kTN * MT) : "memory");
   }
 }
 
-template <int EPI>
+template <int EPI, int MT>
 nmx_status_t launch_gemm(Ctx* c, const CUtensorMap& tm, const CUtensorMap& tw, const GemmArgs& g, dim3 grid) {
   static std::mutex mu;
   static std::map<int, bool> set;
-  const size_t smem = size_t(kTS) * kStageBytes + size_t(kRS) * kRawBytes + 1024;
+  const size_t smem = TcStages<MT>::kSmem;
+  static_assert(TcStages<MT>::kSmem <= 227 * 1024, "prefill GEMM shared memory");
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!set[c->device]) {
-      NMX_CUDA_OK(cudaFuncSetAttribute(qgemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+      NMX_CUDA_OK(
+          cudaFuncSetAttribute(qgemm_tc_kernel<EPI, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
       set[c->device] = true;
     }
   }
-  return launch(c, qgemm_tc_kernel<EPI>, grid, dim3(kGThreads), smem, tm, tw, g);
+  return launch(c, qgemm_tc_kernel<EPI, MT>, grid, dim3(kGThreads), smem, tm, tw, g);
+}
+// two x sub-tiles per CTA (each dequantized weight stage feeds both) once
+// the second sub-tile holds at least half a tile of rows
+template <int EPI>
+nmx_status_t launch_gemm_mt(Ctx* c, const CUtensorMap& tm, const CUtensorMap& tw, const GemmArgs& g, int ntiles) {
+  if (g.M >= kTM + kTM / 2)
+    return launch_gemm<EPI, 2>(c, tm, tw, g, dim3((g.M + 2 * kTM - 1) / (2 * kTM), ntiles));
+  return launch_gemm<EPI, 1>(c, tm, tw, g, dim3((g.M + kTM - 1) / kTM, ntiles));
 }
 
 }  // namespace
@@ -343,13 +367,11 @@ nmx_status_t qgemm_tc(Ctx* c, const GemvDLArgs& a, int epi) {
   g.res = static_cast<const half*>(a.res);
   g.ldres = a.ldres;
   g.err = a.err;
-  const int mt = (a.M + kTM - 1) / kTM;
   const int ntiles = epi == EPI_SILU ? a.N / 128 : a.N / kTN;
-  const dim3 grid(mt, ntiles);
   switch (epi) {
-    case EPI_STORE: return launch_gemm<EPI_STORE>(c, tm, tw, g, grid);
-    case EPI_RESID: return launch_gemm<EPI_RESID>(c, tm, tw, g, grid);
-    default: return launch_gemm<EPI_SILU>(c, tm, tw, g, grid);
+    case EPI_STORE: return launch_gemm_mt<EPI_STORE>(c, tm, tw, g, ntiles);
+    case EPI_RESID: return launch_gemm_mt<EPI_RESID>(c, tm, tw, g, ntiles);
+    default: return launch_gemm_mt<EPI_SILU>(c, tm, tw, g, ntiles);
   }
 }
 
