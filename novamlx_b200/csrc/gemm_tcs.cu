@@ -55,7 +55,7 @@ using tc::mbar_wait;
 using tc::sa_;
 using tc::smem_desc;
 
-constexpr int kDG = 4;                      // dequant warpgroups (they take units in turn)
+constexpr int kDG = 4;                      // dequant warpgroups (3 or 4 of them take units in turn)
 constexpr int kSDW = 4 * kDG;               // dequant / epilogue warps
 constexpr int kNIMax = 4;                   // MMA-issuing warps (one per dequant warpgroup at most)
 constexpr int kSThreads = (kSDW + kNIMax + 2) * 32;  // + MMA-issue, x-tile and record-loader warps
@@ -64,7 +64,7 @@ constexpr int kAST = 4;                     // dequantized weight stages, in TME
 constexpr int kAStageCols = 64;             // 128 k of f16, two per 32-bit column
 constexpr int kAccCols = 512 - kAST * kAStageCols;  // accumulator columns
 constexpr int kXSMax = 8;                   // x stages
-constexpr int kRSMax = 16;                  // raw record slots
+constexpr int kRSMax = 24;                  // raw record slots
 using tc::kRecPad;                          // shared-memory stride of a record
 constexpr int kRawSlot = 8 * kRecPad;       // the 8 records of one tile and K block
 constexpr int kMaxTG = 16;                  // weight tiles per CTA
@@ -76,7 +76,8 @@ struct TcsArgs {
   int M, NT, K, nb;        // rows of x, MMA N, K, K / 128
   int n_atiles;            // weight tiles (SiLU: 2 per output tile)
   int tg, S;               // tiles per group, K shares
-  int ni;                  // MMA-issuing warps (divides 4 and tg)
+  int ndg;                 // dequant warpgroups taking units (3 or 4; each owns A stage dg)
+  int ni;                  // MMA-issuing warps (divides ndg and tg)
   int rs, xs;              // raw slots, x stages
   uint32_t idesc;
   long long pair_tiles;    // SiLU: 16-row tile offset of the up rows
@@ -344,7 +345,7 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
   } else if (warp >= kSWMma && warp < kSWMma + kNIMax) {
     // ------------------------------------------------------------ MMA issue
     // Issuer j (lane 0 of warp kSWMma + j) takes the units i ≡ j (mod ni):
-    // the tiles ti ≡ j and the A stages i mod 4 ≡ j (mod ni), so every
+    // the tiles ti ≡ j and the A stages i mod ndg ≡ j (mod ni), so every
     // accumulator and every A stage has one issuer. An issuing thread pays
     // tens of cycles per tcgen05.mma, so one thread alone caps the tensor
     // pipe; ni threads keep up to ni instruction streams in flight.
@@ -375,8 +376,8 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
                      k16 ? 1u : first);
         tc::mma_commit(&a_empty[as]);
         as += ni;
-        if (as >= kAST) {
-          as -= kAST;
+        if (as >= a.ndg) {
+          as -= a.ndg;
           aph ^= 1;
         }
         ti += ni;
@@ -394,8 +395,8 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
     }
   } else if (warp < kSDW) {
     // ------------------------------------------------ dequantize the tiles
-    // warpgroup dg takes units dg, dg + kDG, ...; thread: TMEM lane L (the
-    // warp's lane quarter), both groups of weight row lane_row(L)
+    // warpgroup dg < ndg takes units dg, dg + ndg, ...; thread: TMEM lane L
+    // (the warp's lane quarter), both groups of weight row lane_row(L)
     const int dg = warp >> 2, L = 32 * (warp & 3) + lane;
     int r8, g16;
     lane_row(L, r8, g16);
@@ -403,9 +404,9 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
     const int sboff = r8 * kRecPad + 1024 + (g16 & 7) * 4 + (g16 >> 3) * 2;
     const uint32_t lane_base = taddr + (uint32_t(32 * (warp & 3)) << 16);
     static_assert(kDG == kAST, "warpgroup dg owns A stage dg");
-    const int as = dg;
+    const int as = dg, ndg = a.ndg;
     int rs = dg % a.rs, rph = (dg / a.rs) & 1;
-    for (int i = dg; i < units; i += kDG) {
+    for (int i = dg; dg < ndg && i < units; i += ndg) {
       // waits agreed over the warp: its lanes arrive together (warp_arrive)
       if (!__all_sync(0xffffffffu, mbar_wait(&raw_full[rs], rph, lim))) {
         atomicOr(a.err, kErrPipeWait);
@@ -430,7 +431,7 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
       tc::warp_arrive(&raw_empty[rs]);  // the slot's bytes are in registers
       // only the TMEM stores wait for the stage's previous MMAs: the loads
       // and the dequantisation above overlap them
-      if (!__all_sync(0xffffffffu, i < kAST || mbar_wait(&a_empty[as], ((i / kAST) - 1) & 1, lim))) {
+      if (!__all_sync(0xffffffffu, i < ndg || mbar_wait(&a_empty[as], ((i / ndg) - 1) & 1, lim))) {
         atomicOr(a.err, kErrPipeWait);
         s_fail = 1;
         break;
@@ -442,7 +443,7 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc::tc_fence_before();
       tc::warp_arrive(&a_full[as]);
-      rs += kDG;
+      rs += ndg;
       while (rs >= a.rs) {
         rs -= a.rs;
         rph ^= 1;
@@ -601,7 +602,7 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
 }
 
 struct TcsPlan {
-  int NT = 0, tg = 0, groups = 0, S = 0, rs = 0, xs = 0, ni = 1;
+  int NT = 0, tg = 0, groups = 0, S = 0, rs = 0, xs = 0, ni = 1, ndg = 4;
   size_t smem = 0, partial_floats = 0;
 };
 
@@ -625,9 +626,11 @@ TcsPlan plan_tcs(int M, int N_out, int K, int epi, int num_sms) {
       const long long waves = (ctas + num_sms - 1) / num_sms;
       if (waves > 1 && S > 1) break;
       const int upc = tga * ((nb + S - 1) / S);
-      const int ni = tga % 4 == 0 ? 4 : (tga % 2 == 0 ? 2 : 1);
+      // warpgroups and issuers: four and four, three and three, four and two
+      const int ndg = tga % 4 == 0 ? 4 : (tga % 3 == 0 ? 3 : 4);
+      const int ni = tga % 4 == 0 ? 4 : (tga % 3 == 0 ? 3 : (tga % 2 == 0 ? 2 : 1));
       // (more issuers also shorten each unit's hand-over: a small preference)
-      const double issue = std::max(1.0, 1.9 / ni) * (1.0 + 0.03 * (4 / ni - 1));
+      const double issue = std::max(1.0, 1.9 / ni) * (1.0 + 0.03 * (4.0 / ni - 1.0));
       const double x_cost = 0.5 * double(p.NT) * 256.0 / (double(tga) * 8 * kRecG);
       const double p_cost = S > 1 ? 0.5 * double(tga) * p.NT * 128 * 8 / (double(upc) * 8 * kRecG) : 0.0;
       const double cost = double(waves) * upc * (issue + x_cost + p_cost) + 1e-6 * double(ctas);
@@ -637,22 +640,22 @@ TcsPlan plan_tcs(int M, int N_out, int K, int epi, int num_sms) {
         p.groups = groups;
         p.S = S;
         p.ni = ni;
+        p.ndg = ndg;
       }
     }
   }
-  // Shared memory: eight raw record slots first, then as many x stages as
-  // fit (up to kXSMax), then more raw slots. An x tile comes from L2 and a
-  // block of tg units can take less time than that round trip, so the x
-  // ring, not the records, sets the pace when it is shallow (two stages at
-  // three tiles per group measured half the MMA-issue rate). The four
+  // Shared memory: three x stages (an x tile comes from L2; two stages at
+  // three tiles per group measured half the MMA-issue rate), the rest raw
+  // record slots: a record copy lands ~5 us after it is issued under a full
+  // load, so the ring's depth sets how many units stream at once. The ndg
   // dequantising warpgroups take units round-robin from the raw ring, so it
-  // holds a multiple of kDG slots: the unit a warpgroup waits for then reuses
+  // holds a multiple of ndg slots: the unit a warpgroup waits for then reuses
   // a slot whose previous unit it consumed itself, and a phase-parity wait
   // can never run two phases ahead.
   const size_t xstage = size_t(2) * p.NT * 128;
-  p.xs = std::max(2, std::min(kXSMax, int((kSmemCap - 1024 - 2 * kDG * size_t(kRawSlot)) / xstage)));
+  p.xs = 3;
   const size_t fixed = size_t(p.xs) * xstage + 1024;
-  p.rs = int(std::min<size_t>(kRSMax, (kSmemCap - fixed) / kRawSlot)) / kDG * kDG;
+  p.rs = int(std::min<size_t>(kRSMax, (kSmemCap - fixed) / kRawSlot)) / p.ndg * p.ndg;
   p.smem = fixed + size_t(p.rs) * kRawSlot;
   p.partial_floats = p.S > 1 ? size_t(p.groups) * p.S * p.tg * p.NT * 128 : 0;
   return p;
@@ -698,7 +701,8 @@ nmx_status_t qgemm_tcs(Ctx* c, const GemvDLArgs& a, int epi) {
             "qgemm_tcs: x must be 16-byte aligned with a 16-byte row pitch");
   NMX_CHECK(reinterpret_cast<uintptr_t>(a.w) % 16 == 0, NMX_ERR_INVALID, "qgemm_tcs: records must be 16-byte aligned");
   const TcsPlan p = plan_tcs(a.M, a.N, a.K, epi, c->num_sms);
-  NMX_CHECK(p.rs >= kDG && p.rs % kDG == 0 && p.smem <= kSmemCap, NMX_ERR_UNSUPPORTED,
+  NMX_CHECK(p.rs >= p.ndg && p.rs % p.ndg == 0 && p.ni >= 1 && p.ndg % p.ni == 0 && p.smem <= kSmemCap,
+            NMX_ERR_UNSUPPORTED,
             "qgemm_tcs: shared-memory plan does not fit");
   if (p.S > 1) {
     NMX_CHECK(a.partials != nullptr && a.partials_cap >= p.partial_floats && a.counters != nullptr,
@@ -718,6 +722,7 @@ nmx_status_t qgemm_tcs(Ctx* c, const GemvDLArgs& a, int epi) {
   g.tg = p.tg;
   g.S = p.S;
   g.ni = p.ni;
+  g.ndg = p.ndg;
   g.rs = p.rs;
   g.xs = p.xs;
   g.idesc = tc::idesc_f16(128, p.NT);
