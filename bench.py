@@ -565,27 +565,35 @@ def run_c4(args, rank, world, dist, torch, nmx, ctx, peaks, dev, clk_box):
         res = torch.zeros_like(part)
         o = torch.empty_like(part)
         reps = 200
-        for _ in range(10):
-            comm.allreduce_resid(part, res, o)
-        torch.cuda.synchronize()
-        _barrier(dist)
-        e0.record()
-        for _ in range(reps):
-            comm.allreduce_resid(part, res, o)
-        e1.record()
-        torch.cuda.synchronize()
-        ours_us = _max_over_ranks(torch, dist, e0.elapsed_time(e1) * 1000.0 / reps)
+
+        def per_call_us(fn, stream):
+            # device time per call: the calls replayed from one CUDA graph
+            # (as in the decode step), so host launch cost is not measured
+            with torch.cuda.stream(stream):
+                for _ in range(10):
+                    fn()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for _ in range(reps):
+                    fn()
+            torch.cuda.synchronize()
+            _barrier(dist)
+            with torch.cuda.stream(stream):
+                g.replay()
+                torch.cuda.synchronize()
+                _barrier(dist)
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
+            torch.cuda.synchronize()
+            t = e0.elapsed_time(e1) * 1000.0 / reps
+            del g
+            return _max_over_ranks(torch, dist, t)
+
+        ours_us = per_call_us(lambda: comm.allreduce_resid(part, res, o), ctx.stream)
         nc = part.clone()
-        for _ in range(10):
-            dist.all_reduce(nc)
-        torch.cuda.synchronize()
-        _barrier(dist)
-        e0.record()
-        for _ in range(reps):
-            dist.all_reduce(nc)
-        e1.record()
-        torch.cuda.synchronize()
-        nccl_us = _max_over_ranks(torch, dist, e0.elapsed_time(e1) * 1000.0 / reps)
+        nccl_us = per_call_us(lambda: dist.all_reduce(nc), torch.cuda.Stream())
         out["exchange"] = {"bytes": C4_BATCH * cfg.hidden * 2, "ours_us_per_call": round(ours_us, 2),
                            "nccl_allreduce_us_per_call": round(nccl_us, 2), "calls_per_step_token": 128,
                            "ours_share_estimate": round(128 * C4_GEN * args.steps * ours_us / 1000.0 / ms, 4),

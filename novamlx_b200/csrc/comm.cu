@@ -17,7 +17,8 @@
 //      (one system-scope fence, then plain stores over NVLink: a release
 //      store per peer serialised a fence per peer);
 //   2. every CTA waits (bounded) until all peers' flags in its own arena
-//      reach e, then one system-scope fence orders its reads after them;
+//      reach e (relaxed polls, then one acquire load of each flag orders its
+//      reads after them);
 //   3. each thread sums the partials of ranks 0..t-1 (peer loads, fixed rank
 //      order, f32) plus the residual and writes the new hidden row — the
 //      same bits on every rank;
@@ -65,6 +66,11 @@ __device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned* p) {
   return v;
 }
 __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 __global__ void __launch_bounds__(kARThreads) allreduce_resid_kernel(ARArgs a) {
   __shared__ unsigned s_e;
@@ -90,9 +96,11 @@ __global__ void __launch_bounds__(kARThreads) allreduce_resid_kernel(ARArgs a) {
           break;
         }
       }
+      // an acquire load of the flag once it is seen: the peer's partial,
+      // written before its release of the flag, is visible to this thread,
+      // and to the CTA's other threads after the barrier below
+      if (ok) (void)ld_acquire_sys(a.my_flags + q);
     }
-    // every flag seen: the peers' partials written before them are visible
-    fence_acq_rel_sys();
     s_ok = ok;
   }
   __syncthreads();
