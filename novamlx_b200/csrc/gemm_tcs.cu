@@ -656,6 +656,13 @@ TcsPlan plan_tcs(int M, int N_out, int K, int epi, int num_sms) {
   p.xs = 3;
   const size_t fixed = size_t(p.xs) * xstage + 1024;
   p.rs = int(std::min<size_t>(kRSMax, (kSmemCap - fixed) / kRawSlot)) / p.ndg * p.ndg;
+  // a CTA with few units needs no more slots than units: the smaller
+  // footprint lets it become resident (and start streaming its weights,
+  // which may be read before the launch wait) while the previous kernel's
+  // last CTAs still hold part of the SM
+  const int upc_max = p.tg * ((nb + p.S - 1) / p.S);
+  const int rs_need = (upc_max + p.ndg - 1) / p.ndg * p.ndg;
+  p.rs = std::max(p.ndg, std::min(p.rs, rs_need));
   p.smem = fixed + size_t(p.rs) * kRawSlot;
   p.partial_floats = p.S > 1 ? size_t(p.groups) * p.S * p.tg * p.NT * 128 : 0;
   return p;
