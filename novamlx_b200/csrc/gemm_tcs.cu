@@ -9,21 +9,24 @@
 // gate/up pairs: both halves of an output tile sit in one TMEM lane) and a
 // contiguous share of the K blocks (128 k); the grid is (groups × S
 // K-shares), sized by the host to one wave over the SMs. Per K block:
-//   * warp 18 brings the 8 records of each of the group's tiles into a ring
+//   * warp 21 brings the 8 records of each of the group's tiles into a ring
 //     of raw slots with ONE 3-d tensor copy per tile (a copy per record
 //     costs more issue time than its bytes take to arrive); these are
 //     weights, so the copies may start before the programmatic-launch wait;
-//   * warp 17 loads the block's x tile once for the whole group (two TMA
-//     boxes of 64 k × NT rows, SWIZZLE_128B, rows past M read as zeros);
-//   * four warpgroups (warps 0-15) take the (block, tile) units in turn:
-//     each thread reads one weight row of the unit (64 bytes, conflict-free:
-//     see lane_row) and writes its 128 f16 weights w = s·q + b straight into
-//     its TMEM lane with tcgen05.st, into one of four 64-column A stages, so
-//     the dequantized tile never touches shared memory;
-//   * one thread of warp 16 issues eight tcgen05.mma (A from TMEM, x from
-//     shared memory; M = 128, N = NT, K = 16) per unit into that tile's
-//     accumulator (TMEM columns tile·NT ...), committing the A stage (and
-//     after the group's last tile the x tile) back to its producers.
+//   * warp 20 loads the block's x tile once for the whole group (two TMA
+//     boxes of 64 k × NT rows, SWIZZLE_128B, rows past M read as zeros) and
+//     warp 22 permutes it in place to the dequantizers' k order (see
+//     dequant_row_words);
+//   * three or four warpgroups (warps 0-15) take the (block, tile) units in
+//     turn: each thread reads one weight row of the unit (64 bytes,
+//     conflict-free: see lane_row) and writes its 128 f16 weights w = s·q + b
+//     straight into its TMEM lane with tcgen05.st, into its warpgroup's
+//     64-column A stage, so the dequantized tile never touches shared memory;
+//   * lane 0 of warps 16-19 (up to four issuers; issuer j owns the tiles and
+//     A stages ≡ j) issues eight tcgen05.mma (A from TMEM, x from shared
+//     memory; M = 128, N = NT, K = 16) per unit into that tile's accumulator
+//     (TMEM columns tile·NT ...), committing the A stage (and after its last
+//     tile of the block the x tile) back to its producers.
 // After the last block warps 0-15 read the accumulators (tcgen05.ld 32x32b;
 // warp w: lanes 32 (w % 4) .., every fourth 8-column chunk). With one K share they run
 // the epilogue directly; with S shares each CTA stores its f32 partial
@@ -58,8 +61,8 @@ using tc::smem_desc;
 constexpr int kDG = 4;                      // dequant warpgroups (3 or 4 of them take units in turn)
 constexpr int kSDW = 4 * kDG;               // dequant / epilogue warps
 constexpr int kNIMax = 4;                   // MMA-issuing warps (one per dequant warpgroup at most)
-constexpr int kSThreads = (kSDW + kNIMax + 2) * 32;  // + MMA-issue, x-tile and record-loader warps
-constexpr int kSWMma = kSDW, kSWTma = kSDW + kNIMax, kSWRec = kSDW + kNIMax + 1;
+constexpr int kSThreads = (kSDW + kNIMax + 3) * 32;  // + MMA-issue, x-tile, record-loader, x-permute warps
+constexpr int kSWMma = kSDW, kSWTma = kSDW + kNIMax, kSWRec = kSDW + kNIMax + 1, kSWPerm = kSDW + kNIMax + 2;
 constexpr int kAST = 4;                     // dequantized weight stages, in TMEM
 constexpr int kAStageCols = 64;             // 128 k of f16, two per 32-bit column
 constexpr int kAccCols = 512 - kAST * kAStageCols;  // accumulator columns
@@ -198,7 +201,11 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
 }
 
 // the 16 words of one record row (both groups) as 128 f16 weights
-// w = s·q + b, two per 32-bit column in k order: group gi in out[gi]
+// w = s·q + b, two per 32-bit column: group gi in out[gi]. XP: word w's
+// eight weights fill columns 4w .. 4w+3 as (w0, w4), (w1, w5), (w2, w6),
+// (w3, w7), the order the nibble step makes them in, and the x block is
+// permuted to match; otherwise in k order (four byte permutes per word).
+template <bool XP>
 __device__ __forceinline__ void dequant_row_words(const uint4* c, __half2 s2[2], __half2 s16[2], __half2 b2[2],
                                                   uint32_t out[2][32]) {
   const __half2 k1024 = __float2half2_rn(1024.f);
@@ -218,16 +225,23 @@ __device__ __forceinline__ void dequant_row_words(const uint4* c, __half2 s2[2],
         __half2 v3 = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&P[3]), k1024), s16[gi], b2[gi]);
         const uint32_t u0 = *reinterpret_cast<uint32_t*>(&v0), u1 = *reinterpret_cast<uint32_t*>(&v1);
         const uint32_t u2 = *reinterpret_cast<uint32_t*>(&v2), u3 = *reinterpret_cast<uint32_t*>(&v3);
-        out[gi][4 * w + 0] = __byte_perm(u0, u1, 0x5410);  // w0, w1
-        out[gi][4 * w + 1] = __byte_perm(u2, u3, 0x5410);  // w2, w3
-        out[gi][4 * w + 2] = __byte_perm(u0, u1, 0x7632);  // w4, w5
-        out[gi][4 * w + 3] = __byte_perm(u2, u3, 0x7632);  // w6, w7
+        if constexpr (XP) {
+          out[gi][4 * w + 0] = u0;
+          out[gi][4 * w + 1] = u1;
+          out[gi][4 * w + 2] = u2;
+          out[gi][4 * w + 3] = u3;
+        } else {
+          out[gi][4 * w + 0] = __byte_perm(u0, u1, 0x5410);  // w0, w1
+          out[gi][4 * w + 1] = __byte_perm(u2, u3, 0x5410);  // w2, w3
+          out[gi][4 * w + 2] = __byte_perm(u0, u1, 0x7632);  // w4, w5
+          out[gi][4 * w + 3] = __byte_perm(u2, u3, 0x7632);  // w6, w7
+        }
       }
     }
   }
 }
 
-template <int EPI>
+template <int EPI, bool XP>
 __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_constant__ CUtensorMap tmap_x,
                                                                   const __grid_constant__ CUtensorMap tmap_w,
                                                                   TcsArgs a) {
@@ -239,6 +253,7 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
   __shared__ __align__(8) uint64_t a_empty[kAST];
   __shared__ __align__(8) uint64_t x_full[kXSMax];
   __shared__ __align__(8) uint64_t x_empty[kXSMax];
+  __shared__ __align__(8) uint64_t x_ready[kXSMax];  // the x block is in the dequantizer's k order
   __shared__ __align__(8) uint64_t raw_full[kRSMax];
   __shared__ __align__(8) uint64_t raw_empty[kRSMax];
   __shared__ __align__(8) uint64_t acc_bar;
@@ -271,6 +286,7 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
     }
     for (int s = 0; s < kXSMax; ++s) {
       mbar_init(&x_full[s], 1);
+      mbar_init(&x_ready[s], 1);  // the x-permute warp (warp_arrive)
       mbar_init(&x_empty[s], ni);  // each issuer, after its last tile of the block
     }
     for (int s = 0; s < kRSMax; ++s) {
@@ -342,6 +358,35 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
         }
       }
     }
+  } else if (warp == kSWPerm) {
+    // ------------------------------------------- x blocks in the k order of A
+    // The dequantizers write each record word's eight weights as the pairs
+    // (w0, w4), (w1, w5), (w2, w6), (w3, w7) — the order the nibble-to-f16
+    // step produces them in — so the x block is put in the same order: in
+    // every 16-byte chunk (8 consecutive k; the 128-byte swizzle only moves
+    // whole chunks) halves 0..7 become 0, 4, 1, 5, 2, 6, 3, 7.
+    int xs = 0, xph = 0;
+    const int chunks = 2 * xhalf / 16;
+    for (int bi = 0; bi < nblk; ++bi) {
+      if (!__all_sync(0xffffffffu, !s_fail && mbar_wait(&x_full[xs], xph, lim))) {
+        atomicOr(a.err, kErrPipeWait);
+        s_fail = 1;
+        break;
+      }
+      uint4* st = reinterpret_cast<uint4*>(stX + xs * 2 * xhalf);
+      for (int c = lane; XP && c < chunks; c += 32) {
+        const uint4 v = st[c];
+        st[c] = make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.x, v.z, 0x7632), __byte_perm(v.y, v.w, 0x5410),
+                           __byte_perm(v.y, v.w, 0x7632));
+      }
+      // generic-proxy writes, read by the tensor core's async proxy
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc::warp_arrive(&x_ready[xs]);
+      if (++xs == a.xs) {
+        xs = 0;
+        xph ^= 1;
+      }
+    }
   } else if (warp >= kSWMma && warp < kSWMma + kNIMax) {
     // ------------------------------------------------------------ MMA issue
     // Issuer j (lane 0 of warp kSWMma + j) takes the units i ≡ j (mod ni):
@@ -359,7 +404,7 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
       int ti = j, as = j, aph = 0, xs = 0, xph = 0;
       uint32_t first = 0u;  // 0 until the first block is in the accumulators
       for (int i = j; i < units; i += ni) {
-        bool ok = !(ti == j && !mbar_wait(&x_full[xs], xph, lim));
+        bool ok = !(ti == j && !mbar_wait(&x_ready[xs], xph, lim));
         if (ok && !mbar_wait(&a_full[as], aph, lim)) ok = false;
         if (!ok) {
           atomicOr(a.err, kErrPipeWait);
@@ -427,7 +472,7 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
         b2[gi] = __halves2half2(bi, bi);
       }
       uint32_t out[2][32];
-      dequant_row_words(c, s2, s16, b2, out);
+      dequant_row_words<XP>(c, s2, s16, b2, out);
       tc::warp_arrive(&raw_empty[rs]);  // the slot's bytes are in registers
       // only the TMEM stores wait for the stage's previous MMAs: the loads
       // and the dequantisation above overlap them
@@ -668,19 +713,26 @@ TcsPlan plan_tcs(int M, int N_out, int K, int epi, int num_sms) {
   return p;
 }
 
-template <int EPI>
-nmx_status_t launch_tcs(Ctx* c, const CUtensorMap& tm, const CUtensorMap& tw, const TcsArgs& g, const TcsPlan& p) {
+template <int EPI, bool XP>
+nmx_status_t launch_tcs_xp(Ctx* c, const CUtensorMap& tm, const CUtensorMap& tw, const TcsArgs& g, const TcsPlan& p) {
   static std::mutex mu;
   static std::map<int, bool> set;
   {
     std::lock_guard<std::mutex> lk(mu);
     if (!set[c->device]) {
-      NMX_CUDA_OK(cudaFuncSetAttribute(qgemm_tcs_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      NMX_CUDA_OK(cudaFuncSetAttribute(qgemm_tcs_kernel<EPI, XP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        int(kSmemCap)));
       set[c->device] = true;
     }
   }
-  return launch(c, qgemm_tcs_kernel<EPI>, dim3(p.groups, p.S), dim3(kSThreads), p.smem, tm, tw, g);
+  return launch(c, qgemm_tcs_kernel<EPI, XP>, dim3(p.groups, p.S), dim3(kSThreads), p.smem, tm, tw, g);
+}
+// The x permute (one warp, once per K block of a CTA) pays off while an x
+// block is small against the units it feeds: up to 64 rows. Wider x blocks
+// keep the byte permutes in the dequantizers.
+template <int EPI>
+nmx_status_t launch_tcs(Ctx* c, const CUtensorMap& tm, const CUtensorMap& tw, const TcsArgs& g, const TcsPlan& p) {
+  return p.NT <= 64 ? launch_tcs_xp<EPI, true>(c, tm, tw, g, p) : launch_tcs_xp<EPI, false>(c, tm, tw, g, p);
 }
 
 }  // namespace
