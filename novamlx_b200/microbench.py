@@ -8,6 +8,7 @@
   python -m novamlx_b200.microbench serve [--layers 32] [--seqs 64] [--tokens 256]
   python -m novamlx_b200.microbench spec [--batch 16] [--ctx 4096] [--drafts 4] [--cycles 8] [--oracle-draft]
   torchrun --nproc-per-node T -m novamlx_b200.microbench tp [--batch 32] [--ctx 8192] [--steps 16] [--prefill 8192]
+  torchrun --nproc-per-node T -m novamlx_b200.microbench spectp [--batch 16] [--ctx 4096] [--drafts 4] [--cycles 8]
 
 gemv: the decode-record GEMV (nmx_op_qmatmul_records) over `copies` distinct
 weight copies, so the weights come from HBM on every launch.
@@ -42,6 +43,11 @@ own greedy continuation (computed before the timed cycles) for the
 full-acceptance verify throughput. The pages before --ctx are left as
 allocated (zeros): the timed work, reading ctx positions of K/V per row, is
 the same as after a real prefill.
+
+spectp: the same speculative decoding with the target tensor-parallel over
+the ranks of torch.distributed.run and the draft sharded by sequence (each
+rank drafts batch / N sequences with its own draft copy; the drafts are
+all-gathered, then every rank verifies all sequences on its target shard).
 
 tp: tensor-parallel decode of the Qwen2.5-32B-style architecture (random
 4-bit weights, --layers layers) over the ranks of torch.distributed.run (one
@@ -301,6 +307,93 @@ def spec(ctx, torch, nmx, batch, ctx_len, n_drafts, cycles, layers, draft_layers
             "target_weight_bytes": target.step_weight_bytes, "draft_weight_bytes": draft.step_weight_bytes}
 
 
+def spec_tp(torch, nmx, batch, ctx_len, n_drafts, cycles, layers, draft_layers):
+    """Speculative decoding with the 70B-style target tensor-parallel over
+    the ranks of torch.distributed.run and the 1B-style draft sharded by
+    sequence: rank r drafts sequences r·B/N .. (r+1)·B/N - 1 with its own
+    copy of the draft (its own KV pool), the drafts are all-gathered (host
+    ids over the process group), and every rank runs the same verify forward
+    of all B sequences on its shard of the target (the exchange makes the
+    results identical on every rank). Timed by wall clock per cycle, the
+    maximum over ranks."""
+    import numpy as np
+    import os
+    import torch.distributed as dist
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        dist.init_process_group("gloo", init_method="env://")
+    if batch % world:
+        raise ValueError("the batch must divide by the number of ranks")
+    torch.cuda.set_device(rank)
+    ctx = nmx.Context(rank)
+    D, bl = n_drafts, batch // world
+    tcfg = nmx.llama33_70b(n_layers=layers, max_batch=batch, max_tokens=batch * (D + 1))
+    target = nmx.Model(ctx, nmx.tp_config(tcfg, world) if world > 1 else tcfg)
+    target.init_random(seed=rank, std=0.02)
+    comm = None
+    if world > 1:
+        comm = nmx.tp_comm(ctx, rank, world, batch * (D + 1) * tcfg.hidden * 2, nmx.torch_exchange(dist))
+        target.set_comm(comm)
+    dcfg = nmx.llama32_1b(n_layers=draft_layers, max_batch=bl, max_tokens=bl)
+    draft = nmx.Model(ctx, dcfg)
+    draft.init_random(seed=1, std=0.02)
+    span = ctx_len + (cycles + 2) * (D + 1) + 16
+    nblk = (span + 15) // 16
+    tables = np.arange(1, batch * nblk + 1, dtype=np.int32).reshape(batch, nblk)
+    dtables = np.arange(1, bl * nblk + 1, dtype=np.int32).reshape(bl, nblk)
+    tpool = nmx.KVPool(target, batch * nblk + 2)
+    dpool = nmx.KVPool(draft, bl * nblk + 2)
+    last0 = np.random.default_rng(0).integers(0, tcfg.vocab, batch).astype(np.int32)
+    mine = slice(rank * bl, (rank + 1) * bl)
+
+    def gather(d_local):
+        # [D, bl] per rank -> [D, batch] on every rank
+        if world == 1:
+            return d_local
+        t = torch.from_numpy(np.ascontiguousarray(d_local.astype(np.int32)))
+        parts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(parts, t)
+        return np.concatenate([p.numpy() for p in parts], axis=1)
+
+    def run(n_cycles):
+        last = last0.copy()
+        pos = np.full(batch, ctx_len, np.int64)
+        emitted = accepted = 0
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(n_cycles):
+            d = gather(draft.decode_greedy(dpool, last[mine], pos[mine].tolist(), dtables, D))
+            seqs = [dict(last_token=int(last[b]), drafts=d[:, b].tolist(), start_pos=int(pos[b]),
+                         block_table=tables[b]) for b in range(batch)]
+            res = nmx.spec_verify(target, tpool, seqs, nmx.VERIFY_PREFIX)
+            for b, (toks, acc) in enumerate(res):
+                emitted += len(toks)
+                accepted += acc
+                pos[b] += 1 + acc
+                last[b] = toks[-1]
+        torch.cuda.synchronize()
+        wall = torch.tensor([time.perf_counter() - t0], dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(wall, op=dist.ReduceOp.MAX)
+        return float(wall[0]), emitted, accepted
+
+    run(1)  # warm-up: graphs and kernel attributes
+    wall, emitted, accepted = run(cycles)
+    out = {"what": "speculative decoding, tensor-parallel target, draft sharded by sequence", "tp": world,
+           "target_layers": layers, "draft_layers": draft_layers, "batch": batch, "ctx": ctx_len, "drafts": D,
+           "cycles": cycles, "ms_per_cycle": round(wall * 1000.0 / cycles, 3), "tok_s": round(emitted / wall, 1),
+           "acceptance": round(accepted / (cycles * batch * D), 4),
+           "target_weight_bytes_per_rank": target.step_weight_bytes, "draft_weight_bytes": draft.step_weight_bytes}
+    if world > 1:
+        target.set_comm(None)
+        comm.close()
+        dist.barrier()
+        dist.destroy_process_group()
+    return out if rank == 0 else None
+
+
 def tp(torch, nmx, batch, ctx_len, steps, layers, prefill, fuse=False):
     import numpy as np
     import os
@@ -368,7 +461,7 @@ def main():
     from novamlx_b200 import nmx
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemv", "qmm", "gemm", "attn", "decode", "serve", "spec", "tp"])
+    ap.add_argument("what", choices=["gemv", "qmm", "gemm", "attn", "decode", "serve", "spec", "spectp", "tp"])
     ap.add_argument("--n", type=int, default=None, help="gemv: 28672, gemm: 4096")
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--m", type=int, default=None, help="gemv: 1, gemm: 2048")
@@ -392,13 +485,19 @@ def main():
     if a.copies is None:
         a.copies = 1 if a.what == "gemm" else 3
     if a.layers is None:
-        a.layers = {"serve": 32, "spec": 80, "tp": 64}.get(a.what, 2)
+        a.layers = {"serve": 32, "spec": 80, "spectp": 80, "tp": 64}.get(a.what, 2)
     if a.tokens is None:
         a.tokens = 256 if a.what == "serve" else 64
     if a.n is None:
         a.n = 4096 if a.what == "gemm" else 28672
     if a.m is None:
         a.m = 2048 if a.what == "gemm" else 1
+    if a.what == "spectp":
+        r = spec_tp(torch, nmx, a.batch if a.batch != 1 else 16, a.ctx if a.ctx != 2048 else 4096, a.drafts,
+                    a.cycles, a.layers, a.draft_layers)
+        if r is not None:
+            print(json.dumps(r), flush=True)
+        return
     if a.what == "tp":
         r = tp(torch, nmx, a.batch if a.batch != 1 else 32, a.ctx if a.ctx != 2048 else 8192, a.steps, a.layers,
                a.prefill, a.fuse)
