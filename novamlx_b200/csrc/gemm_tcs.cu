@@ -279,22 +279,26 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
   unsigned char* stX = smem;
   unsigned char* raw = stX + a.xs * 2 * xhalf;
 
-  if (tid == 0) {
-    for (int s = 0; s < kAST; ++s) {
-      mbar_init(&a_full[s], 4);  // the four warps of one dequant warpgroup per unit
-      mbar_init(&a_empty[s], 1);
+  static_assert(kAST <= 32 && kXSMax <= 32 && kRSMax <= 32, "one barrier of each ring per lane");
+  if (warp == 0) {
+    // the lanes of warp 0 initialise the rings' barriers side by side
+    if (lane < kAST) {
+      mbar_init(&a_full[lane], 4);  // the four warps of one dequant warpgroup per unit
+      mbar_init(&a_empty[lane], 1);
     }
-    for (int s = 0; s < kXSMax; ++s) {
-      mbar_init(&x_full[s], 1);
-      mbar_init(&x_ready[s], 1);  // the x-permute warp (warp_arrive)
-      mbar_init(&x_empty[s], ni);  // each issuer, after its last tile of the block
+    if (lane < kXSMax) {
+      mbar_init(&x_full[lane], 1);
+      mbar_init(&x_ready[lane], 1);   // the x-permute warp (warp_arrive)
+      mbar_init(&x_empty[lane], ni);  // each issuer, after its last tile of the block
     }
-    for (int s = 0; s < kRSMax; ++s) {
-      mbar_init(&raw_full[s], 1);
-      mbar_init(&raw_empty[s], 4);
+    if (lane < kRSMax) {
+      mbar_init(&raw_full[lane], 1);
+      mbar_init(&raw_empty[lane], 4);
     }
-    mbar_init(&acc_bar, ni);
-    s_fail = 0;
+    if (lane == 0) {
+      mbar_init(&acc_bar, ni);
+      s_fail = 0;
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == kSWMma) {
@@ -557,12 +561,14 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
             if (c0 + j < a.M) __stcg(P + ((size_t)ti * NT + c0 + j) * 128 + tlane, v[j]);
         }
       }
-      __threadfence();
       dq_bar();
       if (tid == 0) {
         // every share's partials are in place (the grid is one wave, so the
-        // other shares are resident or done; the wait is bounded)
+        // other shares are resident or done; the wait is bounded). The
+        // barrier above orders the CTA's partial stores before this
+        // thread's fence, which releases them with the count.
         unsigned* ctr = a.counters + grp;
+        __threadfence();
         atomicAdd(ctr, 1u);
         unsigned v = 0;
         for (unsigned it = 0; it < lim; ++it) {
