@@ -152,7 +152,27 @@ __global__ void argmax_kernel(const void* logits, int V, int* out, const int* re
   }
   float bv = -INFINITY;
   int bi = 0x7fffffff;
-  for (int v = threadIdx.x; v < V; v += blockDim.x) {
+  int v0 = 0;  // first id of the scalar loop
+  if constexpr (!PEN && sizeof(T) == 2) {
+    // 16-bit logits, rows on 16-byte boundaries: eight ids per load
+    const uint4* rp = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(logits) + long(row) * V);
+    if (V % 8 == 0 && (reinterpret_cast<uintptr_t>(rp) & 15) == 0) {
+      for (int v8 = threadIdx.x; v8 < V / 8; v8 += blockDim.x) {
+        const uint4 w = rp[v8];
+        const T* h = reinterpret_cast<const T*>(&w);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float x = tof<T>(h[j]);
+          if (better(x, 8 * v8 + j, bv, bi)) {
+            bv = x;
+            bi = 8 * v8 + j;
+          }
+        }
+      }
+      v0 = V;
+    }
+  }
+  for (int v = v0 + threadIdx.x; v < V; v += blockDim.x) {
     float x = ld_logit<T>(logits, long(row) * V + v);
     if (PEN) {
       // count occurrences by binary search for the first and last match
