@@ -102,6 +102,9 @@ def test_qmatmul_c1_config(env):
     (16, 512, 1024, 4, 64), (32, 256, 512, 4, 64), (40, 128, 512, 4, 64),
     (1, 1024, 1024, 8, 64), (4, 512, 2048, 8, 32), (7, 256, 1024, 8, 128), (24, 256, 512, 8, 64),
     (1, 640, 3456, 4, 64),  # a TP8 down-proj shard (54 groups: ragged k-split)
+    (8, 1024, 4096, 4, 64),  # eight activation rows, the most the few-row kernel takes
+    (5, 512, 8192, 4, 128),  # g128: eight 128-k steps per warp
+    (4, 256, 14336, 4, 32),  # g32: fourteen 128-k steps per warp
 ])
 def test_qmatmul_shapes(env, M, N, K, bits, gs):
     torch, nmx, ctx = env
