@@ -592,13 +592,27 @@ __global__ void __launch_bounds__(kSThreads, 1) qgemm_tcs_kernel(const __grid_co
         const int r4 = e & 31, m = (e >> 5) % a.M, ti = ((e >> 5) / a.M) * STEP;
         const float* base = Pg + ((size_t)ti * NT + m) * 128 + 4 * r4;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f), up = acc;
+        if constexpr (EPI == EPI_SILU) {
 #pragma unroll 4
-        for (int sh = 0; sh < a.S; ++sh) {
-          const float4 v = __ldcg(reinterpret_cast<const float4*>(base + sh * share_stride));
-          acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
-          if constexpr (EPI == EPI_SILU) {
+          for (int sh = 0; sh < a.S; ++sh) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(base + sh * share_stride));
             const float4 u = __ldcg(reinterpret_cast<const float4*>(base + NT * 128 + sh * share_stride));
+            acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
             up.x += u.x; up.y += u.y; up.z += u.z; up.w += u.w;
+          }
+        } else {
+          // eight shares' loads in flight at once (one L2 round trip per
+          // eight shares), then added in share order
+          for (int s0 = 0; s0 < a.S; s0 += 8) {
+            float4 v[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              if (s0 + q < a.S) v[q] = __ldcg(reinterpret_cast<const float4*>(base + (s0 + q) * share_stride));
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              if (s0 + q < a.S) {
+                acc.x += v[q].x; acc.y += v[q].y; acc.z += v[q].z; acc.w += v[q].w;
+              }
           }
         }
         const long n0 = (EPI == EPI_SILU ? (long)((t0 + ti) >> 1) : (long)(t0 + ti)) * 128;
