@@ -399,10 +399,11 @@ class Context:
         return out
 
     def paged_decode_attention(self, q, k_cache, v_cache, block_tables, seq_lens, n_kv_heads: int, scale: float,
-                               block_tokens: int = 16):
+                               block_tokens: int = 16, out=None):
         import torch
         B, Hq, D = q.shape
-        out = torch.empty_like(q)
+        if out is None:
+            out = torch.empty_like(q)
         kp = k_cache if isinstance(k_cache, int) else _ptr(k_cache)
         vp = v_cache if isinstance(v_cache, int) else _ptr(v_cache)
         check(self._op(lambda: lib.nmx_op_attn_paged_decode(self.h, _ptr(q), kp, vp, _ptr(block_tables),
