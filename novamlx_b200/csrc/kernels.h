@@ -158,11 +158,23 @@ constexpr int kMaxDecodeSplits = 16;
 constexpr long kMaxDecodeRows = 65535;
 nmx_status_t paged_attention(Ctx* c, const AttnArgs& a, bool fused);
 // key splits per (row, kv head): enough CTAs for two per SM, at most one
-// cluster
+// cluster, and no thin last wave. A CTA keeps only a few pages in flight, so
+// a last wave that fills under half of the SMs' CTA slots streams its pages
+// well below HBM speed (at 4 kv heads × 32 rows, 3 splits made 384 CTAs for
+// 296 slots: 0.84 of HBM; 2 splits, one wave, reach the roofline). Fewer
+// splits are taken until the grid fits one wave or its last wave is at
+// least half full.
 inline int decode_attn_splits(int num_sms, long rows, int Hkv) {
   const long units = rows * long(Hkv > 0 ? Hkv : 1);
-  const long s = (2L * num_sms + units - 1) / units;
-  return int(s < 1 ? 1 : (s > kMaxDecodeSplits ? kMaxDecodeSplits : s));
+  const long slots = 2L * num_sms;
+  long s = (slots + units - 1) / units;
+  s = s < 1 ? 1 : (s > kMaxDecodeSplits ? kMaxDecodeSplits : s);
+  while (s > 1) {
+    const long ctas = units * s, last = ctas % slots;
+    if (ctas <= slots || last == 0 || 2 * last >= slots) break;
+    --s;
+  }
+  return int(s);
 }
 // prefill chunks / mixed batches: query blocks of up to 16 rows of one
 // sequence (attention_prefill.cu). prefill_items cuts the batch's rows
