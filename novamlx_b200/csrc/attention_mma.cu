@@ -28,6 +28,7 @@
 #include <algorithm>
 #include <map>
 #include <mutex>
+#include <tuple>
 
 #include "attn_common.cuh"
 #include "common.cuh"
@@ -649,6 +650,66 @@ nmx_status_t launch_mma(Ctx* c, const AttnArgs& a, int S) {
         s_use = s_use > 8 ? 8 : s_use / 2;
       }
       fit[{c->device, S}] = s_use;
+    }
+  }
+  // The (row, kv head) clusters run in waves of as many clusters as the
+  // device holds at once, which for 9-15 CTAs per cluster is not the CTA
+  // slots over the cluster size (a cluster must fit in one GPC). A last wave
+  // under half full streams its pages well below HBM speed (32 clusters of
+  // 9: a second wave of two, 39 vs ~25 us), so take the largest split count
+  // not above s_use whose clusters fit one wave or leave a last wave at
+  // least half full (none: s_use).
+  static std::map<std::tuple<int, int, long>, int> wave_fit;  // (device, s_use, clusters) → splits
+  const long units = long(a.Hkv) * a.T;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = wave_fit.find({c->device, s_use, units});
+    if (it != wave_fit.end()) {
+      s_use = it->second;
+    } else {
+      auto wave = [&](int s) -> long {  // clusters of s CTAs resident at once
+        if (s == 1) {
+          int per = 0;
+          if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, kAW * 32, smem) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+          }
+          return long(per) * c->num_sms;
+        }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(s, a.Hkv, 1);
+        cfg.blockDim = dim3(kAW * 32);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = s;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+          cudaGetLastError();
+          return 0;
+        }
+        return n;
+      };
+      auto full_enough = [&](int s) {
+        const long n = wave(s);
+        if (n <= 0) return false;
+        const long last = units % n;
+        return units <= n || last == 0 || 2 * last >= n;
+      };
+      int pick = s_use;
+      if (!full_enough(s_use)) {
+        for (int s = s_use - 1; s >= 1; --s)
+          if (full_enough(s)) {
+            pick = s;
+            break;
+          }
+      }
+      wave_fit[{c->device, s_use, units}] = pick;
+      s_use = pick;
     }
   }
   return launch_cluster(c, kern, dim3(s_use, a.Hkv, a.T), dim3(kAW * 32), smem, unsigned(s_use), a);
